@@ -1,0 +1,3 @@
+// Backward selective-scan kernels, bfloat16 activations (float32 state and accumulation).
+#define SSM_ELEM __nv_bfloat16
+#include "ssm_bwd_inst.cuh"

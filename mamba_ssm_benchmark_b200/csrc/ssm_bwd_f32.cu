@@ -1,0 +1,3 @@
+// Backward selective-scan kernels, float32 activations.
+#define SSM_ELEM float
+#include "ssm_bwd_inst.cuh"

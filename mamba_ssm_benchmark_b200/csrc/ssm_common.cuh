@@ -1,0 +1,242 @@
+// ssm_common.cuh — device helpers and launch geometry shared by the selective-scan kernels.
+//
+// Geometry (all kernels): one thread owns 4 consecutive states (n = 4g .. 4g+3) of one
+// channel; N/4 consecutive lanes ("a channel group") cover all N states of a channel, so a
+// warp covers 128/N channels and a CTA of N/4 warps covers DT = 32 channels.  Time is
+// walked sequentially in tiles of TC = 16 steps that TMA stages into shared memory.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ssm {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+enum { kZOH = 0, kEuler = 1, kBilinear = 2 };
+
+template <int N_>
+struct Geo {
+  static constexpr int N = N_;
+  static constexpr int G = 4;              // states per thread
+  static constexpr int LPC = N / G;        // lanes per channel
+  static constexpr int CPW = 32 / LPC;     // channels per warp
+  static constexpr int DT = 32;            // channels per CTA
+  static constexpr int NW = DT / CPW;      // warps per CTA (= N / 4)
+  static constexpr int NT = NW * 32;       // threads per CTA (= 8 N)
+  static constexpr int TC = 16;            // time steps per tile (= checkpoint interval)
+  static_assert(N % G == 0 && LPC >= 1 && LPC <= 16, "N must be 4..64");
+};
+
+constexpr int kChunk = 16;  // checkpoint interval of chunk_states (time steps)
+
+// ------------------------------------------------------------------------------------------
+// Element access
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ float to_f32(float x) { return x; }
+// 4 consecutive elements (16-byte aligned for float, 8-byte aligned for bf16) as float.
+__device__ __forceinline__ void load4(const float* p, float (&o)[4]) {
+  const float4 v = *reinterpret_cast<const float4*>(p);
+  o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+}
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&o)[4]) {
+  const uint2 v = *reinterpret_cast<const uint2*>(p);
+  o[0] = __uint_as_float(v.x << 16); o[1] = __uint_as_float(v.x & 0xffff0000u);
+  o[2] = __uint_as_float(v.y << 16); o[3] = __uint_as_float(v.y & 0xffff0000u);
+}
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+// 2^x on the MUFU unit (flush-to-zero for subnormal results: the decays are in (0, 1]).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// logistic sigmoid from e^-z = 2^(-z log2 e)
+__device__ __forceinline__ float sigmoid(float z) { return rcp(1.0f + ex2(-z * kLog2e)); }
+
+// ------------------------------------------------------------------------------------------
+// Warp transposition-reduce.  v[0..V) hold this lane's partial sums of V quantities; the
+// GROUP lanes {l, l ^ STRIDE, l ^ 2 STRIDE, ...} each contribute one partial per quantity.
+// Recursive halving: at every stage a lane keeps half of its live values and sends the other
+// half to its partner, so V values are reduced over GROUP lanes with (V - V/GROUP) shuffles
+// instead of V log2(GROUP).  On return, with r = (lane / STRIDE) % GROUP:
+//   V >= GROUP: v[0 .. V/GROUP) hold quantities [r V/GROUP, (r+1) V/GROUP)
+//   V <  GROUP: v[0] holds quantity r / (GROUP / V)  (duplicated on GROUP/V lanes)
+// V and GROUP are powers of two.
+// ------------------------------------------------------------------------------------------
+template <int V, int GROUP, int STRIDE>
+__device__ __forceinline__ void xpose_reduce(float (&v)[V], int lane) {
+  static_assert((V & (V - 1)) == 0 && (GROUP & (GROUP - 1)) == 0, "powers of two");
+#pragma unroll
+  for (int stage = 0; (GROUP >> (stage + 1)) >= 1; ++stage) {
+    const int m = (GROUP >> (stage + 1)) * STRIDE;
+    const int K = V >> stage;
+    if (K >= 2) {
+      const int half = K >> 1;
+      const bool upper = (lane & m) != 0;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = upper ? v[i] : v[i + half];
+        const float keep = upper ? v[i + half] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+      }
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], m);
+    }
+  }
+}
+
+// Plain butterfly all-reduce of one value over GROUP lanes spaced STRIDE apart.
+template <int GROUP, int STRIDE>
+__device__ __forceinline__ float group_allreduce(float x) {
+#pragma unroll
+  for (int m = GROUP / 2; m >= 1; m >>= 1) x += __shfl_xor_sync(0xffffffffu, x, m * STRIDE);
+  return x;
+}
+
+// ------------------------------------------------------------------------------------------
+// mbarrier + TMA (cp.async.bulk.tensor) wrappers.  No cluster multicast anywhere.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: gives up after ~2^24 polls (seconds), records the failure in *err and
+// returns, so a copy that never lands ends the kernel with an error flag instead of a hang.
+__device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  for (uint32_t it = 0; it < (1u << 24); ++it) {
+    if (mbar_try_wait(bar, parity)) return;
+  }
+  if (err) atomicOr(err, 1);
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// 3-D tiled TMA load into shared memory, completion signalled on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+// 3-D tiled TMA store from shared memory (out-of-range parts of the box are not written).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int Pending>
+__device__ __forceinline__ void tma_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(Pending) : "memory");
+}
+template <int Pending>
+__device__ __forceinline__ void tma_store_wait_all() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(Pending) : "memory");
+}
+
+// ------------------------------------------------------------------------------------------
+// Kernel parameter blocks (passed as __grid_constant__ so the tensor maps stay addressable)
+// ------------------------------------------------------------------------------------------
+struct DAct {                // (B, rows, cols) tensor with unit column stride
+  const void* ptr;
+  long long sb, sl;          // element strides of batch and row
+};
+
+struct alignas(64) FwdParams {
+  CUtensorMap tm_u, tm_dt, tm_z, tm_B, tm_C, tm_y;
+  DAct u, dt, z, Bm, Cm, y;
+  const float* A;            // (D, N)
+  const float* Dskip;        // (D) or null
+  const float* h_init;       // (B, D, N) or null: state entering t = 0 (segment 0)
+  const float* seg_init;     // (B, S, D, N) or null: state entering each segment (S > 1)
+  float* last;               // (B, D, N) or null
+  float* chunk_states;       // (B, nchunks, D, N) or null
+  float* seg_hend;           // summary mode: (B, S, D, N)
+  float* seg_decay;          // summary mode: (B, S, D, N)
+  int* err;
+  int B, L, D, nchunks, seg_len, nseg;
+  int has_z, use_tma;
+};
+
+struct alignas(64) BwdParams {
+  CUtensorMap tm_u, tm_dt, tm_z, tm_dy, tm_B, tm_C, tm_du, tm_ddt, tm_dz;
+  DAct u, dt, z, dy, Bm, Cm, du, ddt, dz;
+  const float* A;
+  const float* Dskip;
+  const float* h0;           // (B, D, N) or null (only for dh0 presence)
+  const float* chunk_states; // (B, nchunks, D, N)
+  const float* dlast;        // (B, D, N) or null
+  float* dh0;                // (B, D, N) or null
+  float* part_bc;            // (B, nDT, L, 2N): per-CTA dB | dC partial sums
+  float* part_A;             // (B, D, N)
+  float* part_D;             // (B, D)
+  int* err;
+  int B, L, D, nchunks, ndt;
+  int has_z, use_tma;
+};
+
+struct FinParams {
+  const float* part_bc;
+  const float* part_A;
+  const float* part_D;
+  DAct dB, dC;               // outputs (B, L, N), element type T
+  float* dA;                 // (D, N)
+  float* dD;                 // (D) or null
+  int B, L, D, N, ndt;
+};
+
+struct CarryParams {
+  const float* h_init;       // (B, D, N) or null
+  const float* seg_decay;    // (B, S, D, N)
+  const float* seg_hend;     // (B, S, D, N)
+  float* seg_init;           // (B, S, D, N) or null
+  float* tot_decay;          // (B, D, N) or null
+  float* tot_hend;           // (B, D, N) or null
+  int B, D, N, nseg;
+};
+
+struct UpdParams {
+  float* state;              // (B, D, N)
+  DAct x, dt, Bm, Cm, z, y;  // sb used, sl ignored
+  const float* A;
+  const float* Dskip;
+  int B, D, method, has_z;
+};
+
+}  // namespace ssm

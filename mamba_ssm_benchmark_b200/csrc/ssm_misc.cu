@@ -1,0 +1,118 @@
+// ssm_misc.cu — the single-token state update (decode) and the segment-carry kernel.
+#include "ssm_common.cuh"
+
+namespace ssm {
+
+// Sequential composition of per-segment summaries, one thread per (b, d, n):
+//   seg_init[s] = carry;  carry = decay[s] * carry + hend[s]       (s = 0 .. S-1)
+// The chunk-level combine of the reference's two-level scan (models/scan.py:160-164, whose
+// log-depth Hillis-Steele pass over chunk ends is replaced by this O(S) walk per state).
+__global__ void ssm_carry_kernel(const CarryParams p) {
+  const long long dn_total = (long long)p.D * p.N;
+  const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (idx >= (long long)p.B * dn_total) return;
+  const long long b = idx / dn_total, dn = idx % dn_total;
+  float carry = p.h_init != nullptr ? p.h_init[idx] : 0.0f;
+  float dec = 1.0f;
+  const size_t base = (size_t)b * p.nseg * dn_total + dn;
+#pragma unroll 4
+  for (int s = 0; s < p.nseg; ++s) {
+    const size_t o = base + (size_t)s * dn_total;
+    if (p.seg_init != nullptr) p.seg_init[o] = carry;
+    const float a = p.seg_decay[o];
+    carry = fmaf(a, carry, p.seg_hend[o]);
+    dec *= a;
+  }
+  if (p.tot_hend != nullptr) p.tot_hend[idx] = carry;
+  if (p.tot_decay != nullptr) p.tot_decay[idx] = dec;
+}
+
+cudaError_t launch_carry(const CarryParams& p, cudaStream_t stream) {
+  const long long total = (long long)p.B * p.D * p.N;
+  ssm_carry_kernel<<<(unsigned)((total + 127) / 128), 128, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+// Single-token state update: the inline decode branch of Mamba.forward
+// (models/mamba.py:113-118, 123-124).  LPC = N/4 lanes per channel, 4 states per lane.
+template <int N, typename T>
+__global__ void __launch_bounds__(128) ssm_update_kernel(const UpdParams p) {
+  constexpr int LPC = N / 4;
+  const long long gt = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  const long long chn = gt / LPC;
+  const int g = (int)(gt % LPC);
+  const bool valid = chn < (long long)p.B * p.D;
+  const int b = valid ? (int)(chn / p.D) : 0;
+  const int d = valid ? (int)(chn % p.D) : 0;
+  float h[4] = {0.f, 0.f, 0.f, 0.f}, Ak[4] = {-1.f, -1.f, -1.f, -1.f}, Bn[4] = {0.f, 0.f, 0.f, 0.f},
+        Cn[4] = {0.f, 0.f, 0.f, 0.f};
+  float xv = 0.f, dtv = 0.f;
+  float* hp = p.state + ((size_t)b * p.D + d) * N + g * 4;
+  if (valid) {
+    load4(hp, h);
+    load4(p.A + (size_t)d * N + g * 4, Ak);
+    const T* Bm = static_cast<const T*>(p.Bm.ptr) + b * p.Bm.sb + g * 4;
+    const T* Cm = static_cast<const T*>(p.Cm.ptr) + b * p.Cm.sb + g * 4;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      Bn[k] = to_f32(Bm[k]);
+      Cn[k] = to_f32(Cm[k]);
+    }
+    xv = to_f32(static_cast<const T*>(p.x.ptr)[b * p.x.sb + d]);
+    dtv = to_f32(static_cast<const T*>(p.dt.ptr)[b * p.dt.sb + d]);
+  }
+  float acc = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float z = dtv * Ak[k];
+    float a, bb;
+    if (p.method == kZOH) {
+      a = ex2(z * kLog2e);
+      bb = (a - 1.0f) / Ak[k] * (Bn[k] * xv);
+    } else if (p.method == kEuler) {
+      a = ex2(z * kLog2e);
+      bb = dtv * (Bn[k] * xv);
+    } else {
+      const float w = 1.0f / (1.0f - 0.5f * z);
+      a = (1.0f + 0.5f * z) * w;
+      bb = dtv * w * (Bn[k] * xv);
+    }
+    h[k] = fmaf(a, h[k], bb);
+    acc = fmaf(Cn[k], h[k], acc);
+  }
+#pragma unroll
+  for (int m = LPC / 2; m >= 1; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+  if (valid) {
+    *reinterpret_cast<float4*>(hp) = make_float4(h[0], h[1], h[2], h[3]);
+    if (g == 0) {
+      float yv = acc;
+      if (p.Dskip != nullptr) yv = fmaf(p.Dskip[d], xv, yv);
+      if (p.has_z) {
+        const float zz = to_f32(static_cast<const T*>(p.z.ptr)[b * p.z.sb + d]);
+        yv *= zz * sigmoid(zz);
+      }
+      static_cast<T*>(const_cast<void*>(p.y.ptr))[b * p.y.sb + d] = from_f32<T>(yv);
+    }
+  }
+}
+
+template <typename T>
+static cudaError_t launch_update_t(int N, const UpdParams& p, cudaStream_t stream) {
+  const long long threads = (long long)p.B * p.D * (N / 4);
+  const unsigned blocks = (unsigned)((threads + 127) / 128);
+  switch (N) {
+    case 4: ssm_update_kernel<4, T><<<blocks, 128, 0, stream>>>(p); break;
+    case 8: ssm_update_kernel<8, T><<<blocks, 128, 0, stream>>>(p); break;
+    case 16: ssm_update_kernel<16, T><<<blocks, 128, 0, stream>>>(p); break;
+    case 32: ssm_update_kernel<32, T><<<blocks, 128, 0, stream>>>(p); break;
+    case 64: ssm_update_kernel<64, T><<<blocks, 128, 0, stream>>>(p); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_update(int N, bool bf16, const UpdParams& p, cudaStream_t stream) {
+  return bf16 ? launch_update_t<__nv_bfloat16>(N, p, stream) : launch_update_t<float>(N, p, stream);
+}
+
+}  // namespace ssm

@@ -1,0 +1,246 @@
+"""CPU oracle: a restatement of the reference's selective-scan algorithm in plain torch (CPU).
+
+TEST INFRASTRUCTURE ONLY.  Imported by tests/, by __graft_entry__.smoke() and by bench.py's
+CPU-baseline leg as the checker / the timed CPU baseline; never by the product path.
+
+It follows the reference (aman078-ai/mamba-ssm-benchmark) step by step:
+  discretize            models/scan.py:39-55
+  scan_sequential       models/scan.py:70-76
+  scan_hillis_steele    models/scan.py:79-98   (with the h0 fold of :79-84)
+  default_chunk         models/scan.py:138-139
+  scan_chunked          models/scan.py:142-165
+  channel blocks        models/scan.py:180-190
+  ChunkedScanFn         models/scan.py:193-255 (forward + recomputing backward; the
+                        backward's chain rule through discretize, which the reference takes
+                        with autograd at :249, is written out analytically here)
+  selective_scan_loop   models/scan.py:264-274 (autograd through a time loop: ground truth)
+  selective_scan        models/scan.py:277-299 (dtype promotion, autocast off)
+  gate                  models/mamba.py:124
+  state_update          models/mamba.py:113-118
+Parity pin: tests/test_oracle_golden.py checks every function here against golden vectors
+that tests/golden/make_golden.py produced by running the reference's own code.
+"""
+
+import math
+
+import torch
+
+METHODS = ("zoh", "euler", "bilinear")
+# transient (B, L, d_block, N) buffer budget when d_block is not given (models/scan.py:182)
+ELEMENT_BUDGET = 1 << 24
+
+
+def discretize(delta, A, Bm, x, method="zoh"):
+    """(B,L,D) delta, x; (D,N) A; (B,L,N) Bm -> a, b (B,L,D,N)."""
+    z = delta[..., None] * A
+    bx = x[..., None] * Bm[:, :, None, :]
+    if method == "zoh":
+        return torch.exp(z), torch.expm1(z) / A * bx
+    if method == "euler":
+        return torch.exp(z), delta[..., None] * bx
+    if method == "bilinear":
+        w = 1.0 / (1.0 - 0.5 * z)
+        return (1.0 + 0.5 * z) * w, delta[..., None] * w * bx
+    raise ValueError(f"unknown discretization {method!r}")
+
+
+def scan_sequential(a, b, h0=None):
+    """h_t = a_t h_{t-1} + b_t along dim 1, all states returned."""
+    h = torch.zeros_like(b[:, 0]) if h0 is None else h0
+    out = torch.empty_like(b)
+    for t in range(a.shape[1]):
+        h = a[:, t] * h + b[:, t]
+        out[:, t] = h
+    return out
+
+
+def scan_hillis_steele(a, b, h0=None):
+    """Inclusive scan by recursive doubling over dim 1 (h0 folded into the first element)."""
+    if h0 is not None:
+        b = b.clone()
+        b[:, 0] += a[:, 0] * h0
+    n = a.shape[1]
+    step = 1
+    while step < n:
+        b = torch.cat([b[:, :step], b[:, step:] + a[:, step:] * b[:, :-step]], dim=1)
+        if 2 * step < n:
+            a = torch.cat([a[:, :step], a[:, step:] * a[:, :-step]], dim=1)
+        step *= 2
+    return b
+
+
+def default_chunk(L):
+    return max(4, 1 << math.ceil(math.log2(max(1.0, math.sqrt(L)))))
+
+
+def scan_chunked(a, b, h0=None, chunk_size=None):
+    """Two-level scan: sequential inside chunks, doubling scan over chunk ends, fix-up."""
+    Bsz, L = a.shape[:2]
+    rest = tuple(a.shape[2:])
+    C = chunk_size or default_chunk(L)
+    nc = -(-L // C)
+    if nc * C > L:
+        padn = (Bsz, nc * C - L) + rest
+        a = torch.cat([a, a.new_ones(padn)], dim=1)
+        b = torch.cat([b, b.new_zeros(padn)], dim=1)
+    a = a.reshape((Bsz, nc, C) + rest)
+    b = b.reshape((Bsz, nc, C) + rest)
+    local = torch.empty_like(b)
+    local[:, :, 0] = b[:, :, 0]
+    for t in range(1, C):
+        local[:, :, t] = b[:, :, t] + a[:, :, t] * local[:, :, t - 1]
+    decay = torch.cumprod(a, dim=2)
+    ends = scan_hillis_steele(decay[:, :, -1], local[:, :, -1], h0)
+    first = torch.zeros_like(ends[:, :1]) if h0 is None else h0[:, None]
+    carry = torch.cat([first, ends[:, :-1]], dim=1)
+    h = local + decay * carry[:, :, None]
+    return h.reshape((Bsz, nc * C) + rest)[:, :L]
+
+
+def channel_blocks(B, L, D, N, d_block=None):
+    if not d_block:
+        d_block = max(1, ELEMENT_BUDGET // (B * L * N))
+    d_block = min(d_block, D)
+    return [(i, min(i + d_block, D)) for i in range(0, D, d_block)]
+
+
+def _scan_fn(chunk_size):
+    return lambda a, b, h0=None: scan_chunked(a, b, h0, chunk_size)
+
+
+def discretize_with_partials(delta, A, Bm, x, method="zoh"):
+    """a, b of discretize() plus the partials the backward needs, all (B, L, D, N):
+
+    coef = db/d(B x);  a_d, b_d = da/ddelta, db/ddelta;  a_A, b_A = da/dA, db/dA.
+    ZOH's db/dA uses A db/dA = delta db/ddelta - coef Bx, the exact form of
+    (z e^z - expm1 z) / z^2 that needs no small-z branch.
+    """
+    z = delta[..., None] * A
+    bx = x[..., None] * Bm[:, :, None, :]
+    dt = delta[..., None]
+    if method == "zoh":
+        a = torch.exp(z)
+        coef = torch.expm1(z) / A
+        return a, coef * bx, coef, A * a, a * bx, dt * a, (dt * a - coef) * bx / A
+    if method == "euler":
+        a = torch.exp(z)
+        return a, dt * bx, dt.expand_as(z), A * a, bx, dt * a, torch.zeros_like(z)
+    if method == "bilinear":
+        w = 1.0 / (1.0 - 0.5 * z)
+        w2 = w * w
+        return (1.0 + 0.5 * z) * w, dt * w * bx, dt * w, A * w2, w2 * bx, dt * w2, 0.5 * dt * dt * w2 * bx
+    raise ValueError(f"unknown discretization {method!r}")
+
+
+class ChunkedScanFn(torch.autograd.Function):
+    """Memory-bounded selective scan: saves only the inputs; the backward recomputes the states
+    of one channel block at a time with the chunked scan, runs the adjoint recurrence
+    dh_t = g_t + a_{t+1} dh_{t+1} as a reversed chunked scan, and applies the chain rule
+    through the discretisation analytically."""
+
+    @staticmethod
+    def forward(ctx, x, delta, A, Bm, Cm, h0, method, d_block, chunk_size):
+        scan = _scan_fn(chunk_size)
+        Bsz, L, D = x.shape
+        N = A.shape[1]
+        y = torch.empty_like(x)
+        last = x.new_empty(Bsz, D, N)
+        for i, j in channel_blocks(Bsz, L, D, N, d_block):
+            a, b = discretize(delta[..., i:j], A[i:j], Bm, x[..., i:j], method)
+            h = scan(a, b, None if h0 is None else h0[:, i:j])
+            y[..., i:j] = torch.einsum("bldn,bln->bld", h, Cm)
+            last[:, i:j] = h[:, -1]
+        ctx.save_for_backward(x, delta, A, Bm, Cm, h0)
+        ctx.cfg = (method, d_block, chunk_size)
+        return y, last
+
+    @staticmethod
+    def backward(ctx, dy, dlast):
+        x, delta, A, Bm, Cm, h0 = ctx.saved_tensors
+        method, d_block, chunk_size = ctx.cfg
+        scan = _scan_fn(chunk_size)
+        Bsz, L, D = x.shape
+        N = A.shape[1]
+        grads = dict(x=torch.empty_like(x), delta=torch.empty_like(delta), A=torch.empty_like(A),
+                     B=torch.zeros_like(Bm), C=torch.zeros_like(Cm),
+                     h0=None if h0 is None else torch.empty_like(h0))
+        for i, j in channel_blocks(Bsz, L, D, N, d_block):
+            xb, hb0 = x[..., i:j], (None if h0 is None else h0[:, i:j])
+            a, b, coef, a_d, b_d, a_A, b_A = discretize_with_partials(delta[..., i:j], A[i:j], Bm, xb, method)
+            h = scan(a, b, hb0)
+            dyb = dy[..., i:j]
+            grads["C"] += torch.einsum("bld,bldn->bln", dyb, h)
+            g = dyb[..., None] * Cm[:, :, None, :]
+            if dlast is not None:
+                g[:, -1] += dlast[:, i:j]
+            a_shift = torch.cat([a[:, 1:], torch.ones_like(a[:, :1])], dim=1)
+            dh = scan(a_shift.flip(1), g.flip(1)).flip(1)
+            start = torch.zeros_like(h[:, :1]) if hb0 is None else hb0[:, None]
+            hp = torch.cat([start, h[:, :-1]], dim=1)
+            grads["delta"][..., i:j] = (dh * (hp * a_d + b_d)).sum(-1)
+            grads["A"][i:j] = (dh * (hp * a_A + b_A)).sum((0, 1))
+            dhc = dh * coef
+            grads["B"] += torch.einsum("bldn,bld->bln", dhc, xb)
+            grads["x"][..., i:j] = torch.einsum("bldn,bln->bld", dhc, Bm)
+            if hb0 is not None:
+                grads["h0"][:, i:j] = dh[:, 0] * a[:, 0]
+        return (grads["x"], grads["delta"], grads["A"], grads["B"], grads["C"], grads["h0"], None, None, None)
+
+
+def selective_scan_loop(x, delta, A, Bm, Cm, h0=None, method="zoh"):
+    """Ground truth: time loop differentiated by autograd (O(B L D N) memory; small shapes)."""
+    Bsz, L, D = x.shape
+    h = x.new_zeros(Bsz, D, A.shape[1]) if h0 is None else h0
+    ys = []
+    for t in range(L):
+        a, b = discretize(delta[:, t:t + 1], A, Bm[:, t:t + 1], x[:, t:t + 1], method)
+        h = a[:, 0] * h + b[:, 0]
+        ys.append(torch.einsum("bdn,bn->bd", h, Cm[:, t]))
+    return torch.stack(ys, 1), h
+
+
+def selective_scan(x, delta, A, Bm, Cm, h0=None, method="zoh", scan="chunked", d_block=None, chunk_size=None):
+    """(y, last) computed in promote(x.dtype, float32) like the reference; y cast back to x.dtype."""
+    dtype = x.dtype
+    ct = torch.promote_types(dtype, torch.float32)
+    with torch.autocast(device_type=x.device.type, enabled=False):
+        args = [None if t is None else t.to(ct) for t in (x, delta, A, Bm, Cm, h0)]
+        if scan == "reference":
+            y, last = selective_scan_loop(*args, method=method)
+        elif scan == "chunked":
+            y, last = ChunkedScanFn.apply(*args, method, d_block, chunk_size)
+        else:
+            raise ValueError(f"oracle implements scan='chunked' and 'reference', not {scan!r}")
+    return y.to(dtype), last
+
+
+def gate(y, x, Dskip=None, z=None):
+    """Mamba mixer output before out_proj: (y + x D) * silu(z)."""
+    if Dskip is not None:
+        y = y + x * Dskip.to(x.dtype)
+    if z is not None:
+        y = y * torch.nn.functional.silu(z)
+    return y
+
+
+def selective_scan_fused(x, delta, A, Bm, Cm, h0=None, method="zoh", Dskip=None, z=None, **kw):
+    y, last = selective_scan(x, delta, A, Bm, Cm, h0=h0, method=method, **kw)
+    return gate(y, x, Dskip, z), last
+
+
+def state_update(state, x, delta, A, Bm, Cm, Dskip=None, z=None, method="zoh"):
+    """One decode step; returns (y (B, D), new state).  x, delta, z: (B, D); Bm, Cm: (B, N)."""
+    ct = state.dtype
+    a, b = discretize(delta[:, None].to(ct), A.to(ct), Bm[:, None].to(ct), x[:, None].to(ct), method)
+    h = a[:, 0] * state + b[:, 0]
+    y = torch.einsum("bdn,bn->bd", h, Cm.to(ct))
+    y = gate(y.to(x.dtype), x, Dskip, z)
+    return y, h
+
+
+def normwise_error(got, ref):
+    """max |got - ref| / max |ref| (elementwise relative error is meaningless near zeros)."""
+    got = got.detach().double().cpu()
+    ref = ref.detach().double().cpu()
+    den = ref.abs().max().item()
+    return (got - ref).abs().max().item() / (den if den > 0 else 1.0)

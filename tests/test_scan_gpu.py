@@ -1,0 +1,218 @@
+"""GPU parity of the sm_100a selective scan (called through the C ABI) against the reference.
+
+Mirrors the reference's own GPU tests (tests/test_triton.py, tests/test_gpu.py) with the
+oracle as the reference implementation, plus golden vectors the reference itself produced.
+"""
+
+import pytest
+import torch
+
+import scan_harness as H
+from conftest import golden_names, load_golden
+from mamba_ssm_benchmark_b200 import _native as nat
+from mamba_ssm_benchmark_b200 import selective_scan, selective_scan_fused, selective_scan_triton
+from mamba_ssm_benchmark_b200.workloads import make_inputs
+from oracle import scan_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+METHODS = ("zoh", "euler", "bilinear")
+
+
+@pytest.fixture(autouse=True)
+def _no_device_errors():
+    yield
+    assert nat.read_device_error() == 0, "a kernel gave up on a bounded wait"
+
+
+# ---- golden vectors produced by the reference (models/scan.py, fp32 chunked) ---------------
+@pytest.mark.parametrize("name", golden_names("scan_"))
+def test_matches_reference_golden_vectors(name):
+    case = load_golden(name)
+    method = next(m for m in METHODS if f"_{m}" in name)
+    ins = dict(u=case["u"], delta=case["delta"], A=case["A"], Bm=case["Bm"], Cm=case["Cm"], h0=case.get("h0"),
+               Dskip=None, z=None, dy=case["w1"])
+    got = H.run(H.ours, ins, method, DEV, torch.float32, "h0" in case, False, w1=case["w1"], w2=case["w2"])
+    ref = {k: case[k] for k in ("y", "last", "du", "ddelta", "dA", "dBm", "dCm") if k in case}
+    if "dh0" in case:
+        ref["dh0"] = case["dh0"]
+    H.compare(got, ref)
+
+
+@pytest.mark.parametrize("name", golden_names("loop_"))
+def test_matches_float64_ground_truth(name):
+    case = load_golden(name)
+    method = next(m for m in METHODS if f"_{m}" in name)
+    ins = dict(u=case["u"], delta=case["delta"], A=case["A"], Bm=case["Bm"], Cm=case["Cm"], h0=case["h0"],
+               Dskip=None, z=None, dy=case["w1"])
+    got = H.run(H.ours, ins, method, DEV, torch.float32, True, False, w1=case["w1"], w2=case["w2"])
+    H.compare(got, {k: case[k] for k in ("y", "last", "du", "ddelta", "dA", "dBm", "dCm", "dh0")})
+
+
+def test_fused_config_distribution_golden():
+    case = load_golden("fused_cfg.npz")
+    out, last = selective_scan_fused(*(case[k].to(DEV) for k in ("u", "delta", "A", "Bm", "Cm")),
+                                     D=case["Dskip"].to(DEV), z=case["z"].to(DEV))
+    assert O.normwise_error(out, case["out"]) < H.FWD_TOL
+    assert O.normwise_error(last, case["last"]) < H.FWD_TOL
+
+
+# ---- oracle differential tests on the reference's GPU test shapes and edge cases -----------
+SHAPES = [(2, 1, 32, 16), (2, 37, 50, 16), (3, 130, 96, 8), (2, 77, 40, 16), (1, 300, 64, 4), (2, 45, 33, 32),
+          (1, 40, 16, 64), (4, 16, 32, 16), (1, 17, 1, 16)]
+
+
+@pytest.mark.parametrize("method", METHODS)
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("h0", [False, True])
+@pytest.mark.parametrize("fused", [False, True])
+def test_matches_oracle(method, shape, h0, fused):
+    ins = make_inputs(*shape, seed=sum(shape), dist="test", h0=h0, dlast=True)
+    w2 = ins["dlast"]
+    got = H.run(H.ours, ins, method, DEV, torch.float32, h0, fused, w2=w2)
+    ref = H.run(H.oracle, ins, method, "cpu", torch.float32, h0, fused, w2=w2)
+    H.compare(got, ref)
+
+
+@pytest.mark.parametrize("method", METHODS)
+def test_config_distribution_mid_size(method):
+    """Config-0/1 input distributions (delta ~ 0.01, A = -(n+1)) with the fused gate."""
+    ins = make_inputs(4, 512, 128, 16, seed=3, dist="config")
+    got = H.run(H.ours, ins, method, DEV, torch.float32, False, True)
+    ref = H.run(H.oracle, ins, method, "cpu", torch.float32, False, True)
+    H.compare(got, ref, elementwise=False)
+
+
+def test_config1_full_size_forward_backward():
+    """BASELINE config 1 at its full size: B=16, L=512, D=512, N=16, fp32, fused."""
+    ins = make_inputs(16, 512, 512, 16, seed=0, dist="config")
+    got = H.run(H.ours, ins, "zoh", DEV, torch.float32, False, True)
+    ref = H.run(H.oracle, ins, "zoh", "cpu", torch.float32, False, True)
+    errs = H.compare(got, ref, elementwise=False)
+    print("config1 normwise errors:", {k: f"{v:.2e}" for k, v in errs.items()})
+
+
+def test_config0_full_size_forward():
+    """B=1, L=4096, D=512, N=16 forward (sequence split across CTAs)."""
+    ins = make_inputs(1, 4096, 512, 16, seed=0, dist="config")
+    got = H.run(H.ours, ins, "zoh", DEV, torch.float32, False, True, grads=False)
+    ref = H.run(H.oracle, ins, "zoh", "cpu", torch.float32, False, True, grads=False)
+    H.compare(got, ref, elementwise=False)
+
+
+def test_long_sequence_matches_chunked():
+    """tests/test_gpu.py:80-88: L = 8192, D = 64, no grad, 1e-3."""
+    ins = make_inputs(1, 8192, 64, 16, seed=0, dist="test")
+    got = H.run(H.ours, ins, "zoh", DEV, torch.float32, False, False, grads=False)
+    ref = H.run(H.oracle, ins, "zoh", "cpu", torch.float32, False, False, grads=False)
+    torch.testing.assert_close(got["y"].cpu(), ref["y"], rtol=1e-3, atol=1e-3)
+    torch.testing.assert_close(got["last"].cpu(), ref["last"], rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("L", [64, 1000, 4096])
+def test_sequence_split_forward_and_backward(L):
+    """B = 1 and few channels: the forward splits the sequence into segments (summary pass,
+    carry, main pass); the backward consumes the checkpoints the split forward wrote."""
+    ins = make_inputs(1, L, 32, 16, seed=L, dist="config", h0=True)
+    got = H.run(H.ours, ins, "zoh", DEV, torch.float32, True, True)
+    ref = H.run(H.oracle, ins, "zoh", "cpu", torch.float32, True, True)
+    H.compare(got, ref, elementwise=False)
+
+
+def test_extreme_decays_stay_finite():
+    """tests/test_scan.py:132-142 analogue: decays from ~1 - 1e-4 to ~1e-6 over L = 2048."""
+    ins = make_inputs(1, 2048, 32, 16, seed=1, dist="test")
+    ins["delta"][..., :16] = 1e-4 * torch.rand(1, 2048, 16)
+    ins["delta"][..., 16:] = 14.0
+    ins["A"] = -torch.rand(32, 16) * 2 - 1.0
+    got = H.run(H.ours, ins, "zoh", DEV, torch.float32, False, False)
+    ref = H.run(H.oracle, ins, "zoh", "cpu", torch.float32, False, False)
+    H.compare(got, ref, elementwise=False)
+
+
+# ---- dtypes, views, determinism -----------------------------------------------------------
+@pytest.mark.parametrize("shape", [(2, 100, 64, 16), (1, 33, 40, 8)])
+def test_bf16_activations(shape):
+    """Native bf16 loads/stores, fp32 state: compared with the reference run on the same
+    bf16-rounded inputs upcast to fp32."""
+    ins = make_inputs(*shape, seed=5, dist="config", dtype=torch.bfloat16)
+    got = H.run(H.ours, ins, "zoh", DEV, torch.bfloat16, False, True)
+    ins32 = {k: (v.float() if v is not None else None) for k, v in ins.items()}
+    ref = H.run(H.oracle, ins32, "zoh", "cpu", torch.float32, False, True)
+    H.compare(got, ref, fwd_tol=H.BF16_TOL, grad_tol=H.BF16_TOL, elementwise=False)
+    assert got["y"].dtype == torch.bfloat16 and got["last"].dtype == torch.float32
+    assert got["du"].dtype == torch.bfloat16 and got["dA"].dtype == torch.float32
+
+
+def test_mixed_dtypes_are_promoted_like_the_reference():
+    ins = make_inputs(2, 40, 32, 16, seed=9, dist="test")
+    x = ins["u"].to(DEV, torch.bfloat16)
+    args = [ins[k].to(DEV) for k in ("delta", "A", "Bm", "Cm")]
+    y, last = selective_scan(x, *args)
+    yr, lr = O.selective_scan(x.cpu(), *(a.cpu() for a in args))
+    assert y.dtype == torch.bfloat16 and last.dtype == torch.float32
+    assert O.normwise_error(y, yr) < H.BF16_TOL and O.normwise_error(last, lr) < H.FWD_TOL
+
+
+def test_strided_views_tma_and_fallback_paths():
+    """x and z as the two halves of in_proj's output (row stride 2D, TMA path) and as views
+    whose strides TMA cannot describe (D = 50: 200-byte rows, cooperative-load path)."""
+    for D in (64, 50):
+        ins = make_inputs(2, 70, D, 16, seed=D, dist="test")
+        xz = torch.cat([ins["u"], ins["z"]], dim=-1).to(DEV).requires_grad_()
+        x, z = xz.chunk(2, dim=-1)
+        args = [ins[k].to(DEV).requires_grad_() for k in ("delta", "A", "Bm", "Cm")]
+        Dk = ins["Dskip"].to(DEV).requires_grad_()
+        y, last = selective_scan_fused(x, args[0], args[1], args[2], args[3], D=Dk, z=z)
+        g = torch.autograd.grad((y * ins["dy"].to(DEV)).sum(), [xz] + args + [Dk])
+        xr = torch.cat([ins["u"], ins["z"]], dim=-1).requires_grad_()
+        xr_, zr_ = xr.chunk(2, dim=-1)
+        argsr = [ins[k].clone().requires_grad_() for k in ("delta", "A", "Bm", "Cm")]
+        Dr = ins["Dskip"].clone().requires_grad_()
+        yr, lr = O.selective_scan_fused(xr_, *argsr, Dskip=Dr, z=zr_)
+        gr = torch.autograd.grad((yr * ins["dy"]).sum(), [xr] + argsr + [Dr])
+        assert O.normwise_error(y, yr) < H.FWD_TOL
+        for a, b in zip(g, gr):
+            assert O.normwise_error(a, b) < H.GRAD_TOL
+
+
+def test_backward_is_bitwise_deterministic():
+    """tests/test_gpu.py:28-47 analogue, without needing a deterministic mode switch."""
+    ins = make_inputs(3, 300, 96, 16, seed=0, dist="test")
+
+    def grads():
+        lv = H.leaves_of(ins, DEV, torch.float32, False, True)
+        y, _ = selective_scan_fused(lv["u"], lv["delta"], lv["A"], lv["Bm"], lv["Cm"], D=lv["Dskip"], z=lv["z"])
+        return torch.autograd.grad(y.square().sum(), [lv[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dskip", "z")])
+
+    g1, g2 = grads(), grads()
+    for a, b in zip(g1, g2):
+        assert torch.equal(a, b)
+
+
+def test_triton_compatible_entry_point():
+    ins = make_inputs(2, 37, 50, 16, seed=1, dist="test", h0=True)
+    args = [ins[k].to(DEV) for k in ("u", "delta", "A", "Bm", "Cm")]
+    y1, l1 = selective_scan_triton(*args, h0=ins["h0"].to(DEV), method="bilinear", d_block=8)
+    y2, l2 = selective_scan(*args, h0=ins["h0"].to(DEV), method="bilinear", scan="triton")
+    assert torch.equal(y1, y2) and torch.equal(l1, l2)
+
+
+def test_dB_dC_linearity_over_channel_groups():
+    """Size-independent property at a config-3-like width: dB, dC of the full channel range
+    equal the sum of those of disjoint channel groups (the kernel reduces over channels)."""
+    ins = make_inputs(2, 256, 640, 16, seed=4, dist="config", dtype=torch.float32)
+    full = H.run(H.ours, ins, "zoh", DEV, torch.float32, False, True)
+    acc_B = torch.zeros_like(full["dBm"])
+    acc_C = torch.zeros_like(full["dCm"])
+    for lo in range(0, 640, 160):
+        part = {k: v for k, v in ins.items()}
+        for k in ("u", "delta", "z", "dy"):
+            part[k] = ins[k][..., lo:lo + 160]
+        part["A"] = ins["A"][lo:lo + 160]
+        part["Dskip"] = ins["Dskip"][lo:lo + 160]
+        r = H.run(H.ours, part, "zoh", DEV, torch.float32, False, True)
+        acc_B += r["dBm"]
+        acc_C += r["dCm"]
+    assert O.normwise_error(acc_B, full["dBm"]) < 1e-5
+    assert O.normwise_error(acc_C, full["dCm"]) < 1e-5
