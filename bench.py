@@ -1,0 +1,398 @@
+#!/usr/bin/env python
+"""Selective-scan (Mamba S6) fwd+bwd throughput on B200 — the BASELINE config-1 workload.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|3]
+
+One step = the fused selective scan forward + backward over one batch (B=16, L=512, D=512,
+N=16, fp32, with the mixer's D-skip and SiLU(z) gate) through the C ABI of libssm_b200.so.
+Prints one JSON line (rank 0).
+
+value  : whole-job tokens/s with inputs resident in HBM (CUDA events around exactly K steps,
+         barrier + synchronize on both sides, max over ranks).  Input/output sets rotate so
+         that every step touches buffers evicted from the 126 MB L2 (4 sets, ~0.5 GB).
+e2e    : the same metric through the public Python API (selective_scan_fused + autograd
+         backward) with host (pinned) inputs and outputs: H2D copies, fwd, bwd and D2H copies
+         of every output inside the timed region.
+N > 1  : one process per GPU (torchrun).  Channel sharding, weak scaling: every rank owns a
+         512-channel shard of a (512 N)-channel layer; B and C are shared, so the backward
+         ends with an NCCL all-reduce of dB|dC (the real exchange of channel sharding).
+         A token is one (batch, position) row through 512 channels, so the job processes
+         N x B x L tokens per step.
+--impl reference : the reference's CPU scan (the oracle port of models/scan.py, chunked scan +
+         recomputing backward) on the host cores, bounded samples of the same workload.
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "selective-scan fwd+bwd tokens/s and achieved HBM GB/s (% of peak) at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", type=int, choices=(1, 3), default=1)
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(workload):
+    """dram read+write bytes per launch of the backward kernel, from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", f"bwd_kernel_{workload}.md")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+# --------------------------------------------------------------------------------------------
+# clocks during the timed region
+# --------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 7]
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[4:8]) if "Active" in v and "Not" not in v})
+        loaded = [s for s in sm if mx and s > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------------------------
+# the GPU arm
+# --------------------------------------------------------------------------------------------
+class ScanStep:
+    """Pre-marshalled C-ABI calls of one fused fwd+bwd step over one buffer set."""
+
+    def __init__(self, cfg, device, seed, shared_seed, B_rows=None):
+        from mamba_ssm_benchmark_b200 import _native as nat
+        from mamba_ssm_benchmark_b200.workloads import make_inputs
+        self.nat = nat
+        B, L, D, N = cfg.B, cfg.L, cfg.D, cfg.N
+        dt = cfg.dtype
+        ins = make_inputs(B, L, D, N, seed=seed, dist="config", dtype=dt)
+        shared = make_inputs(B, L, D, N, seed=shared_seed, dist="config", dtype=dt)
+        ins["Bm"], ins["Cm"] = shared["Bm"], shared["Cm"]
+        t = {k: (v.to(device) if v is not None else None) for k, v in ins.items()}
+        self.t = t
+        f32 = dict(dtype=torch.float32, device=device)
+        self.y = torch.empty(B, L, D, dtype=dt, device=device)
+        self.last = torch.empty(B, D, N, **f32)
+        self.cs = torch.empty(B, -(-L // 16), D, N, **f32)
+        self.yg = torch.empty(B, L, D, dtype=dt, device=device)
+        self.du = torch.empty(B, L, D, dtype=dt, device=device)
+        self.ddelta = torch.empty_like(self.du)
+        self.dz = torch.empty_like(self.du)
+        self.dBC = torch.empty(B, L, 2 * N, dtype=dt, device=device)   # dB | dC in one buffer
+        self.dA = torch.empty(D, N, **f32)
+        self.dD = torch.empty(D, **f32)
+        self.fws = nat.fwd_workspace_bytes(B, L, D, N)
+        self.bws = nat.bwd_workspace_bytes(B, L, D, N)
+        self.fw = torch.empty(max(self.fws, 1), dtype=torch.uint8, device=device)
+        self.bw = torch.empty(self.bws, dtype=torch.uint8, device=device)
+        v3, p = nat.view3, nat.ptr
+        self.lib = nat.lib()
+        stream = nat.stream_of(device)
+        self.fwd_args = (B, L, D, N, 0, v3(t["u"]), v3(t["delta"]), p(t["A"]), v3(t["Bm"]), v3(t["Cm"]),
+                         p(t["Dskip"]), v3(t["z"]), None, v3(self.y), v3(self.yg), p(self.last), p(self.cs),
+                         self.fw.data_ptr(),
+                         self.fws, stream)
+        self.bwd_args = (B, L, D, N, 0, v3(t["u"]), v3(t["delta"]), p(t["A"]), v3(t["Bm"]), v3(t["Cm"]),
+                         p(t["Dskip"]), v3(t["z"]), None, p(self.cs), v3(self.yg), v3(t["dy"]), None, v3(self.du),
+                         v3(self.ddelta), p(self.dA), v3(self.dBC[..., :N]), v3(self.dBC[..., N:]), p(self.dD),
+                         v3(self.dz), None, self.bw.data_ptr(), self.bws, stream)
+        self.launches = (1 if self.fws == 0 else 3) + 2
+
+    def fwd(self):
+        rc = self.lib.ssm_scan_fwd(*self.fwd_args)
+        if rc:
+            self.nat.check(rc, "ssm_scan_fwd")
+
+    def bwd(self):
+        rc = self.lib.ssm_scan_bwd(*self.bwd_args)
+        if rc:
+            self.nat.check(rc, "ssm_scan_bwd")
+
+
+def e2e_run(cfg, device, steps, world, seed):
+    """Public API with host buffers: H2D + fwd + bwd + D2H of every output, per step."""
+    from mamba_ssm_benchmark_b200 import selective_scan_fused
+    from mamba_ssm_benchmark_b200.workloads import make_inputs
+    ins = make_inputs(cfg.B, cfg.L, cfg.D, cfg.N, seed=seed, dist="config", dtype=cfg.dtype)
+    host = {k: v.pin_memory() for k, v in ins.items() if v is not None}
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    outs_host = None
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        nonlocal outs_host
+        dv = {k: v.to(device, non_blocking=True) for k, v in host.items()}
+        leaves = [dv[k].requires_grad_() for k in ("u", "delta", "A", "Bm", "Cm", "Dskip", "z")]
+        y, last = selective_scan_fused(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4], D=leaves[5],
+                                       z=leaves[6])
+        grads = torch.autograd.grad(y, leaves, dv["dy"])
+        res = [y.detach(), last.detach()] + list(grads)
+        if outs_host is None:
+            outs_host = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+        for o, r in zip(outs_host, res):
+            o.copy_(r, non_blocking=True)
+        return sum(r.numel() * r.element_size() for r in res)
+
+    for _ in range(3):
+        d2h = step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+    return ms / steps, h2d, d2h
+
+
+def cpu_reference_sample(cfg, budget_s, d_slice=None, b_rows=None, repeats_min=3):
+    """Oracle port (the reference's chunked CPU scan + recomputing backward) on a slice of the
+    workload; returns (tokens/s in 512-channel token units, description, samples)."""
+    from mamba_ssm_benchmark_b200.workloads import make_inputs
+    from oracle import scan_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    b = b_rows or cfg.B
+    d = d_slice or cfg.D
+    ins = make_inputs(b, cfg.L, d, cfg.N, seed=0, dist="config", dtype=torch.float32)
+
+    def one():
+        lv = [ins[k].clone().requires_grad_() for k in ("u", "delta", "A", "Bm", "Cm", "Dskip", "z")]
+        y, _ = O.selective_scan_fused(lv[0], lv[1], lv[2], lv[3], lv[4], Dskip=lv[5], z=lv[6])
+        torch.autograd.grad(y, lv, ins["dy"])
+
+    one()
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < repeats_min or time.perf_counter() - t_start < budget_s:
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > 3 * budget_s:
+            break
+    med = statistics.median(times)
+    tokens = b * cfg.L * d / 512.0
+    desc = f"B={b} of {cfg.B} rows, L={cfg.L}, {d} of {cfg.D} channels, N={cfg.N}, fused fwd+bwd; median of {len(times)}"
+    return tokens / med, desc, times
+
+
+def run_reference(args, cfg, workload):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    # size one "step" so that warmup + steps fit in ~150 s of host time
+    from mamba_ssm_benchmark_b200.workloads import make_inputs  # noqa: F401
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    probe_rate, _, probe = cpu_reference_sample(cfg, 0.0, d_slice=min(cfg.D, 64), b_rows=1, repeats_min=1)
+    t_probe = statistics.median(probe)
+    d_s = int(max(8, min(cfg.D, 64 * budget / max(t_probe, 1e-6))) // 8 * 8)
+    b_s = 1
+    if d_s >= cfg.D:
+        d_s = cfg.D
+        b_s = int(max(1, min(cfg.B, budget / max(t_probe * cfg.D / 64, 1e-6))))
+    from oracle import scan_oracle as O
+    from mamba_ssm_benchmark_b200.workloads import make_inputs as mk
+    ins = mk(b_s, cfg.L, d_s, cfg.N, seed=0, dist="config", dtype=torch.float32)
+
+    def step():
+        lv = [ins[k].clone().requires_grad_() for k in ("u", "delta", "A", "Bm", "Cm", "Dskip", "z")]
+        y, _ = O.selective_scan_fused(lv[0], lv[1], lv[2], lv[3], lv[4], Dskip=lv[5], z=lv[6])
+        torch.autograd.grad(y, lv, ins["dy"])
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    tokens = b_s * cfg.L * d_s / 512.0
+    value = tokens * args.steps / dt
+    sample = f"per step: B={b_s} of {cfg.B} rows, L={cfg.L}, {d_s} of {cfg.D} channels, N={cfg.N}, fused fwd+bwd " \
+             f"(tokens counted in 512-channel units)"
+    cores = torch.get_num_threads()
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": workload, "B": cfg.B, "L": cfg.L, "D": cfg.D, "N": cfg.N},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": sample + "; oracle/scan_oracle.py restates models/scan.py (chunked)"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    from mamba_ssm_benchmark_b200.workloads import CONFIGS, algorithmic_bytes
+    cfg = CONFIGS[args.config]
+    workload = cfg.name
+    if args.impl == "reference":
+        run_reference(args, cfg, workload)
+        return
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=device)
+    sets = 4 if args.config == 1 else 1
+    steps = [ScanStep(cfg, device, seed=1000 * s + rank, shared_seed=1000 * s) for s in range(sets)]
+    stream = torch.cuda.current_stream(device)
+    dBC_bufs = [st.dBC for st in steps]
+
+    def one(i, ev=None):
+        st = steps[i % sets]
+        st.fwd()
+        if ev is not None:
+            ev[0].record(stream)
+        st.bwd()
+        if ev is not None:
+            ev[1].record(stream)
+        if world > 1:
+            torch.distributed.all_reduce(dBC_bufs[i % sets])
+
+    for i in range(args.warmup):
+        one(i)
+    torch.cuda.synchronize(device)
+    K = args.steps
+    bev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    clocks = ClockSampler(local)
+    clocks.start()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(K):
+        one(i, bev[i])
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in bev)
+    if world > 1:
+        t = torch.tensor([ms, bwd_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, bwd_ms = t.tolist()
+    ms_step = ms / K
+    tokens_step = cfg.B * cfg.L * world
+    value = tokens_step / (ms_step / 1e3)
+    eb = 4 if cfg.dtype == torch.float32 else 2
+    fwd_bytes, bwd_bytes = algorithmic_bytes(cfg.B, cfg.L, cfg.D, cfg.N, eb, fused=True, backward=True)
+    peak, peak_kind = measured_peak()
+    achieved = bwd_bytes / (bwd_ms / 1e3) / 1e9
+    step_gbs = (fwd_bytes + bwd_bytes) / (ms_step / 1e3) / 1e9
+    traffic = ncu_traffic(workload)
+
+    e2e_ms, h2d, d2h = e2e_run(cfg, device, args.e2e_steps, world, seed=77 + rank)
+    e2e_value = tokens_step / (e2e_ms / 1e3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, desc, _ = cpu_reference_sample(cfg, budget_s=12.0, b_rows=max(1, cfg.B // 8) if cfg.B > 1 else 1,
+                                             d_slice=cfg.D if args.config == 1 else 128)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": desc + "; oracle/scan_oracle.py restates models/scan.py (chunked scan)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": workload, "B": cfg.B, "L": cfg.L, "D_per_gpu": cfg.D, "N": cfg.N,
+                       "activations": str(cfg.dtype).replace("torch.", ""), "fused_gate": True,
+                       "parallelism": f"channel-sharded x{world} (weak)" if world > 1 else "single GPU",
+                       "l2": f"{sets} rotating buffer sets" + (" (>126 MB L2)" if sets > 1 else
+                                                                " (inputs > 126 MB L2)"),
+                       "token": "one (batch, position) row through a 512-channel shard"},
+            "hbm_gbs_step": step_gbs, "hbm_frac_step": step_gbs / peak,
+            "roofline": {"kernel": "ssm_scan_bwd (ssm_bwd_kernel + ssm_bwd_finalize)", "bound": "hbm",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6.65 TB/s", "traffic": traffic,
+                         "algorithmic_bytes_per_launch": bwd_bytes, "avg_launch_ms": bwd_ms},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": args.e2e_steps},
+            "gpu_launches": K * steps[0].launches,
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
+                       "samples": clk["samples"]},
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

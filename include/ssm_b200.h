@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define SSM_B200_ABI_VERSION 1
+#define SSM_B200_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define SSM_API __attribute__((visibility("default")))
@@ -80,6 +80,9 @@ typedef struct {
  * u, delta, z: (B, L, D); Bm, Cm: (B, L, N); A: (D, N); Dskip: (D) or NULL;
  * z.ptr may be NULL; h0: (B, D, N) or NULL (zeros).
  * out y: (B, L, D) view, same dtype as u (models/scan.py:299 returns y.to(x.dtype)).
+ * out ygate: (B, L, D) view or NULL: the gate's input y + Dskip*u before the SiLU(z)
+ *   product.  A training caller passes it when z is given; ssm_scan_bwd needs it to form dz
+ *   without recomputing y (it is the one activation the backward cannot rebuild cheaply).
  * out last: (B, D, N) float32 or NULL (the reference's h_last).
  * out chunk_states: (B, ceil(L/16), D, N) float32 or NULL. When given, the state
  *   entering every 16-step chunk is saved for ssm_scan_bwd (the backward then
@@ -94,7 +97,7 @@ SSM_API int ssm_scan_fwd_workspace_size(int64_t B, int64_t L, int64_t D, int64_t
 SSM_API int ssm_scan_fwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method,
                  ssm_view u, ssm_view delta, const float* A, ssm_view Bm, ssm_view Cm,
                  const float* Dskip, ssm_view z, const float* h0,
-                 ssm_view y, float* last, float* chunk_states,
+                 ssm_view y, ssm_view ygate, float* last, float* chunk_states,
                  void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------
@@ -102,9 +105,9 @@ SSM_API int ssm_scan_fwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t met
  * (kernels/triton_scan.py:143-226, 288-319) and SelectiveScanFn.backward
  * (models/scan.py:219-255).
  *
- * Inputs as in ssm_scan_fwd, plus chunk_states written by the forward call on the
- * same inputs, dy (B, L, D) = gradient of the forward output, dlast (B, D, N) or
- * NULL (zeros; kernels/triton_scan.py:294).
+ * Inputs as in ssm_scan_fwd, plus chunk_states and ygate written by the forward call on
+ * the same inputs (ygate required iff z.ptr != NULL), dy (B, L, D) = gradient of the
+ * forward output, dlast (B, D, N) or NULL (zeros; kernels/triton_scan.py:294).
  * Outputs (all required unless noted):
  *   du, ddelta: (B, L, D) views, dtype of u;  dBm, dCm: (B, L, N) views, dtype of u;
  *   dA: (D, N) float32 (summed over batch, kernels/triton_scan.py:319);
@@ -121,7 +124,7 @@ SSM_API int ssm_scan_bwd_workspace_size(int64_t B, int64_t L, int64_t D, int64_t
 SSM_API int ssm_scan_bwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method,
                  ssm_view u, ssm_view delta, const float* A, ssm_view Bm, ssm_view Cm,
                  const float* Dskip, ssm_view z, const float* h0,
-                 const float* chunk_states, ssm_view dy, const float* dlast,
+                 const float* chunk_states, ssm_view ygate, ssm_view dy, const float* dlast,
                  ssm_view du, ssm_view ddelta, float* dA, ssm_view dBm, ssm_view dCm,
                  float* dDskip, ssm_view dz, float* dh0,
                  void* workspace, size_t workspace_bytes, void* stream);
@@ -133,7 +136,7 @@ SSM_API int ssm_scan_bwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t met
  *   from zero.  Composition of shard summaries is the chunk combine of the
  *   reference's two-level scan (models/scan.py:142-165, step (2)).
  * Phase 2 runs the shard again from the carried-in state h_in (B, D, N) and writes
- * y / last / chunk_states exactly like ssm_scan_fwd with h0 = h_in.
+ * y / ygate / last / chunk_states exactly like ssm_scan_fwd with h0 = h_in.
  * Both phases take the same workspace (ssm_scan_fwd_workspace_size bytes); phase 2
  * reuses the per-block summaries phase 1 left there, so the two calls must use the
  * same workspace and inputs, in order, on the same stream.
@@ -146,7 +149,7 @@ SSM_API int ssm_scan_fwd_summary(int64_t B, int64_t L, int64_t D, int64_t N, int
 SSM_API int ssm_scan_fwd_finish(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method,
                         ssm_view u, ssm_view delta, const float* A, ssm_view Bm, ssm_view Cm,
                         const float* Dskip, ssm_view z, const float* h_in,
-                        ssm_view y, float* last, float* chunk_states,
+                        ssm_view y, ssm_view ygate, float* last, float* chunk_states,
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------

@@ -17,7 +17,7 @@ SSM_OK, SSM_ERR_INVALID, SSM_ERR_DTYPE, SSM_ERR_WORKSPACE, SSM_ERR_CUDA, SSM_ERR
 SSM_F32, SSM_BF16 = 0, 1
 METHODS = {"zoh": 0, "euler": 1, "bilinear": 2}
 DTYPES = {torch.float32: SSM_F32, torch.bfloat16: SSM_BF16}
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # Every symbol include/ssm_b200.h declares (checked by the tests).
 EXPORTED = (
@@ -50,13 +50,13 @@ _SIGNATURES = {
     "ssm_scan_fwd_workspace_size": (ctypes.c_int, [_I64, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
     "ssm_scan_bwd_workspace_size": (ctypes.c_int, [_I64, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
     "ssm_scan_fwd": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _V, _P, _V, _V, _P, _V, _P,
-                                    _V, _P, _P, _P, _SZ, _P]),
+                                    _V, _V, _P, _P, _P, _SZ, _P]),
     "ssm_scan_fwd_summary": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _V, _P, _V, _P, _P,
                                             _P, _SZ, _P]),
     "ssm_scan_fwd_finish": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _V, _P, _V, _V, _P, _V, _P,
-                                           _V, _P, _P, _P, _SZ, _P]),
+                                           _V, _V, _P, _P, _P, _SZ, _P]),
     "ssm_scan_bwd": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _V, _P, _V, _V, _P, _V, _P,
-                                    _P, _V, _P, _V, _V, _P, _V, _V, _P, _V, _P, _P, _SZ, _P]),
+                                    _P, _V, _V, _P, _V, _V, _P, _V, _V, _P, _V, _P, _P, _SZ, _P]),
     "ssm_state_update": (ctypes.c_int, [_I64, _I64, _I64, _I32, _P, _V, _V, _P, _V, _V, _P, _V, _V, _P]),
 }
 

@@ -12,6 +12,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -129,6 +130,20 @@ int sm_count() {
   return n;
 }
 
+// States per thread.  G = 4 keeps more independent recurrences per thread; G = 2 doubles the
+// thread count, which pays off when the (batch x channel) grid at G = 4 would give the GPU
+// fewer than 16 warps per SM (the recurrences are latency-bound at low occupancy).  Built for
+// N = 8 and 16.  SSM_B200_STATES_PER_THREAD=2|4 overrides the choice (tuning, tests).
+int choose_g(int64_t B, int64_t D, int64_t N) {
+  if (N != 8 && N != 16) return 4;
+  if (const char* env = getenv("SSM_B200_STATES_PER_THREAD")) {
+    if (env[0] == '2') return 2;
+    if (env[0] == '4') return 4;
+  }
+  const int64_t threads4 = B * ((D + 31) / 32) * 32 * N / 4;
+  return threads4 < (int64_t)sm_count() * 512 ? 2 : 4;
+}
+
 // Sequence split of the forward: S segments of seg_len steps (a multiple of 16).  Splitting
 // doubles the recurrence work (summary pass + main pass), so it is used only when the
 // (batch x channel-tile) grid alone cannot give every SM a CTA.
@@ -200,8 +215,8 @@ int check_f32(const char* name, const void* p, bool required) {
 // per-segment summaries a phase-1 call left in the workspace).
 int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm_view u, ssm_view delta,
              const float* A, ssm_view Bm, ssm_view Cm, const float* Dskip, ssm_view z, const float* h0,
-             ssm_view y, float* last, float* chunk_states, float* tot_decay, float* tot_hend, void* workspace,
-             size_t workspace_bytes, void* stream_v) {
+             ssm_view y, ssm_view ygate, float* last, float* chunk_states, float* tot_decay, float* tot_hend,
+             void* workspace, size_t workspace_bytes, void* stream_v) {
   int rc = check_common(B, L, D, N, method);
   if (rc) return rc;
   if (u.ptr == nullptr) return fail(SSM_ERR_INVALID, "u is required");
@@ -213,6 +228,7 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
     if ((rc = check_view("Cm", Cm, dt, N, true))) return rc;
     if ((rc = check_view("z", z, dt, D, false))) return rc;
     if ((rc = check_view("y", y, dt, D, true))) return rc;
+    if ((rc = check_view("ygate", ygate, dt, D, false))) return rc;
   }
   if ((rc = check_f32("A", A, true))) return rc;
   if ((rc = check_f32("Dskip", Dskip, false))) return rc;
@@ -234,6 +250,8 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   p.Bm = dact(Bm);
   p.Cm = dact(Cm);
   p.y = dact(y);
+  p.yg = dact(ygate);
+  p.save_ygate = (phase != 1 && ygate.ptr != nullptr) ? 1 : 0;
   p.A = A;
   p.Dskip = Dskip;
   p.last = last;
@@ -246,12 +264,12 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   p.has_z = z.ptr != nullptr;
 
   bool use_tma = tma_ok(u, B, L, D) && tma_ok(delta, B, L, D) && tma_ok(Bm, B, L, N);
-  if (phase != 1) use_tma = use_tma && tma_ok(Cm, B, L, N) && tma_ok(y, B, L, D) && (!p.has_z || tma_ok(z, B, L, D));
+  if (phase != 1) use_tma = use_tma && tma_ok(Cm, B, L, N) && (!p.has_z || tma_ok(z, B, L, D));
   if (use_tma) {
     bool ok = make_map(&p.tm_u, u, B, L, D, 32, kChunk) && make_map(&p.tm_dt, delta, B, L, D, 32, kChunk) &&
               make_map(&p.tm_B, Bm, B, L, N, (int)N, kChunk);
     if (phase != 1) {
-      ok = ok && make_map(&p.tm_C, Cm, B, L, N, (int)N, kChunk) && make_map(&p.tm_y, y, B, L, D, 32, kChunk);
+      ok = ok && make_map(&p.tm_C, Cm, B, L, N, (int)N, kChunk);
       if (p.has_z) ok = ok && make_map(&p.tm_z, z, B, L, D, 32, kChunk);
     }
     use_tma = ok;
@@ -265,9 +283,10 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   const unsigned ndt = (unsigned)((D + 31) / 32);
   const dim3 grid(ndt, (unsigned)S, (unsigned)B);
   const bool bf = dt == SSM_BF16;
+  const int G = choose_g(B, D, N);
   auto launch = [&](int mode, const FwdParams& q) {
-    return bf ? launch_fwd<__nv_bfloat16>((int)N, method, mode, q, grid, stream)
-              : launch_fwd<float>((int)N, method, mode, q, grid, stream);
+    return bf ? launch_fwd<__nv_bfloat16>((int)N, G, method, mode, q, grid, stream)
+              : launch_fwd<float>((int)N, G, method, mode, q, grid, stream);
   };
   cudaError_t e;
 
@@ -354,9 +373,9 @@ int ssm_scan_bwd_workspace_size(int64_t B, int64_t L, int64_t D, int64_t N, size
 
 int ssm_scan_fwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm_view u, ssm_view delta,
                  const float* A, ssm_view Bm, ssm_view Cm, const float* Dskip, ssm_view z, const float* h0,
-                 ssm_view y, float* last, float* chunk_states, void* workspace, size_t workspace_bytes,
-                 void* stream) {
-  return fwd_impl(0, B, L, D, N, method, u, delta, A, Bm, Cm, Dskip, z, h0, y, last, chunk_states, nullptr,
+                 ssm_view y, ssm_view ygate, float* last, float* chunk_states, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  return fwd_impl(0, B, L, D, N, method, u, delta, A, Bm, Cm, Dskip, z, h0, y, ygate, last, chunk_states, nullptr,
                   nullptr, workspace, workspace_bytes, stream);
 }
 
@@ -366,21 +385,22 @@ int ssm_scan_fwd_summary(int64_t B, int64_t L, int64_t D, int64_t N, int32_t met
   ssm_view none;
   memset(&none, 0, sizeof(none));
   none.dtype = u.dtype;
-  return fwd_impl(1, B, L, D, N, method, u, delta, A, Bm, none, nullptr, none, nullptr, none, nullptr, nullptr,
-                  decay, hend, workspace, workspace_bytes, stream);
+  return fwd_impl(1, B, L, D, N, method, u, delta, A, Bm, none, nullptr, none, nullptr, none, none, nullptr,
+                  nullptr, decay, hend, workspace, workspace_bytes, stream);
 }
 
 int ssm_scan_fwd_finish(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm_view u, ssm_view delta,
                         const float* A, ssm_view Bm, ssm_view Cm, const float* Dskip, ssm_view z,
-                        const float* h_in, ssm_view y, float* last, float* chunk_states, void* workspace,
-                        size_t workspace_bytes, void* stream) {
-  return fwd_impl(2, B, L, D, N, method, u, delta, A, Bm, Cm, Dskip, z, h_in, y, last, chunk_states, nullptr,
-                  nullptr, workspace, workspace_bytes, stream);
+                        const float* h_in, ssm_view y, ssm_view ygate, float* last, float* chunk_states,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  return fwd_impl(2, B, L, D, N, method, u, delta, A, Bm, Cm, Dskip, z, h_in, y, ygate, last, chunk_states,
+                  nullptr, nullptr, workspace, workspace_bytes, stream);
 }
 
 int ssm_scan_bwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm_view u, ssm_view delta,
                  const float* A, ssm_view Bm, ssm_view Cm, const float* Dskip, ssm_view z, const float* h0,
-                 const float* chunk_states, ssm_view dy, const float* dlast, ssm_view du, ssm_view ddelta,
+                 const float* chunk_states, ssm_view ygate, ssm_view dy, const float* dlast, ssm_view du,
+                 ssm_view ddelta,
                  float* dA, ssm_view dBm, ssm_view dCm, float* dDskip, ssm_view dz, float* dh0, void* workspace,
                  size_t workspace_bytes, void* stream_v) {
   int rc = check_common(B, L, D, N, method);
@@ -394,6 +414,7 @@ int ssm_scan_bwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm
   if ((rc = check_view("Cm", Cm, dt, N, true))) return rc;
   if ((rc = check_view("z", z, dt, D, false))) return rc;
   if ((rc = check_view("dy", dy, dt, D, true))) return rc;
+  if ((rc = check_view("ygate", ygate, dt, D, has_z))) return rc;
   if ((rc = check_view("du", du, dt, D, true))) return rc;
   if ((rc = check_view("ddelta", ddelta, dt, D, true))) return rc;
   if ((rc = check_view("dBm", dBm, dt, N, true))) return rc;
@@ -419,6 +440,7 @@ int ssm_scan_bwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm
   p.dt = dact(delta);
   p.z = dact(z);
   p.dy = dact(dy);
+  p.yg = dact(ygate);
   p.Bm = dact(Bm);
   p.Cm = dact(Cm);
   p.du = dact(du);
@@ -443,22 +465,21 @@ int ssm_scan_bwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm
   p.part_D = carve(cur, (size_t)B * D);
 
   bool use_tma = tma_ok(u, B, L, D) && tma_ok(delta, B, L, D) && tma_ok(dy, B, L, D) && tma_ok(Bm, B, L, N) &&
-                 tma_ok(Cm, B, L, N) && tma_ok(du, B, L, D) && tma_ok(ddelta, B, L, D) &&
-                 (!has_z || (tma_ok(z, B, L, D) && tma_ok(dz, B, L, D)));
+                 tma_ok(Cm, B, L, N) && (!has_z || (tma_ok(z, B, L, D) && tma_ok(ygate, B, L, D)));
   if (use_tma) {
     bool ok = make_map(&p.tm_u, u, B, L, D, 32, kChunk) && make_map(&p.tm_dt, delta, B, L, D, 32, kChunk) &&
               make_map(&p.tm_dy, dy, B, L, D, 32, kChunk) && make_map(&p.tm_B, Bm, B, L, N, (int)N, kChunk) &&
-              make_map(&p.tm_C, Cm, B, L, N, (int)N, kChunk) && make_map(&p.tm_du, du, B, L, D, 32, kChunk) &&
-              make_map(&p.tm_ddt, ddelta, B, L, D, 32, kChunk);
-    if (has_z) ok = ok && make_map(&p.tm_z, z, B, L, D, 32, kChunk) && make_map(&p.tm_dz, dz, B, L, D, 32, kChunk);
+              make_map(&p.tm_C, Cm, B, L, N, (int)N, kChunk);
+    if (has_z) ok = ok && make_map(&p.tm_z, z, B, L, D, 32, kChunk) && make_map(&p.tm_yg, ygate, B, L, D, 32, kChunk);
     use_tma = ok;
   }
   p.use_tma = use_tma ? 1 : 0;
 
   const bool bf = dt == SSM_BF16;
   const dim3 grid((unsigned)ndt, (unsigned)B, 1);
-  cudaError_t e = bf ? launch_bwd<__nv_bfloat16>((int)N, method, p, grid, stream)
-                     : launch_bwd<float>((int)N, method, p, grid, stream);
+  const int G = choose_g(B, D, N);
+  cudaError_t e = bf ? launch_bwd<__nv_bfloat16>((int)N, G, method, p, grid, stream)
+                     : launch_bwd<float>((int)N, G, method, p, grid, stream);
   if (e != cudaSuccess) return cuda_fail(e, "backward launch");
 
   FinParams f;

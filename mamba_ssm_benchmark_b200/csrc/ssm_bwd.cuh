@@ -6,84 +6,109 @@
 // through discretize).
 //
 // One CTA owns a (batch, 32-channel tile) and walks the sequence backwards in 16-step chunks.
-// For every chunk it (1) TMA-stages u, delta, z, dy and B, C, (2) recomputes the chunk's 16
-// states in registers from the checkpoint the forward saved (chunk_states), (3) runs the
-// reverse adjoint through those registers.  No per-step state ever touches HBM.
+// For every chunk it
+//   (1) TMA-stages u, delta, z, dy, the saved pre-gate output and B, C;
+//   (2) gate pass, once per (t, d): dys = dy silu(z), dz, dD; and four state-permuted fp32
+//       copies of the B, C tiles (see "state permutation" below);
+//   (3) recomputes the chunk's 16 states in registers from the checkpoint the forward saved
+//       (chunk_states), caching the decays a_t in shared memory;
+//   (4) runs the reverse adjoint through those registers.
+// No per-step state ever touches HBM.
 //
 // Per element (t, d, n), with dh the total adjoint of h_t (carried + dys_t C_t[n]):
-//   q = dh a_t              adjoint flowing to h_{t-1}
-//   ddelta_t[d] += sum_n dh dh_t/ddelta,  dA[d,n] += dh dh_t/dA,  du_t[d] += dh dh_t/du
-//   dB_t[n] += sum_d dh dh_t/dB,          dC_t[n] += sum_d dys_t[d] h_t[n]
-// Reductions over n stay inside a channel group (warp shuffles); reductions over d go
-// through a shuffle transposition, a fixed-order cross-warp sum in shared memory and a
-// per-CTA partial buffer that ssm_bwd_finalize sums in fixed order: no float atomics, so
-// gradients are bitwise reproducible.
-//
+//   q = dh a_t                      adjoint flowing to h_{t-1}
+//   ddelta_t[d] += sum_n dh dh_t/ddelta,   du_t[d] += sum_n dh dh_t/du,   dA[d,n] += dh dh_t/dA,
+//   dB_t[n] += sum_d dh dh_t/dB,           dC_t[n] += sum_d dys_t[d] h_t[n]
 // ZOH dA uses the identity  A dh_t/dA = delta dh_t/ddelta - coef B u   (coef = expm1(dA)/A),
 // so no separate small-z series is needed (the reference evaluates
 // f(z) = (z e^z - expm1 z)/z^2 with a series branch, kernels/triton_scan.py:199-202).
+//
+// Reductions: over n inside a channel's lane group (shuffle transposition); over d by a
+// shuffle transposition across the warp's channels, a fixed-order cross-warp sum in shared
+// memory and a per-CTA partial that ssm_bwd_finalize sums in fixed order.  No float atomics:
+// gradients are bitwise reproducible.
+//
+// State permutation: lane c of a channel group keeps its G states in register slots
+// j -> state G g + (j ^ perm(c)), perm taken from the log2(G) highest bits of c.  Then the
+// first log2(G) halving stages of the dB|dC transposition send a fixed register slot on every
+// lane (no lane-dependent selects).  The B, C tiles are staged as G copies, one per perm, so
+// every lane still reads its G values with one vector shared load.
 #pragma once
 
 #include "ssm_common.cuh"
 
+#ifndef SSM_BWD_HSMEM
+#define SSM_BWD_HSMEM 0
+#endif
+
 namespace ssm {
 
-template <int N, typename T>
+template <int N, int G, typename T>
 struct BwdSmem {
-  using Gm = Geo<N>;
+  using Gm = Geo<N, G>;
+  static constexpr int TC = Gm::TC, DT = Gm::DT;
   static constexpr int NSTAGE = 2;
   static constexpr int NOUT = 2;
-  static constexpr int ACT = Gm::TC * Gm::DT * (int)sizeof(T);
-  static constexpr int BC = Gm::TC * N * (int)sizeof(T);
-  static constexpr int OFF_U = 0, OFF_DT = ACT, OFF_Z = 2 * ACT, OFF_DY = 3 * ACT, OFF_B = 4 * ACT,
-                       OFF_C = 4 * ACT + BC;
-  static constexpr int STAGE = 4 * ACT + 2 * BC;
-  static constexpr int F32T = Gm::TC * Gm::DT * 4;                     // one fp32 (16 x 32) tile
-  static constexpr int OFF_DYS = NSTAGE * STAGE;                      // dy * silu(z)
-  static constexpr int OFF_SIG = OFF_DYS + F32T;                      // sigmoid(z)
-  static constexpr int OFF_OUT = OFF_SIG + F32T;                      // NOUT x {du, ddelta, dz}
-  static constexpr int OFF_RED = OFF_OUT + NOUT * 3 * ACT;            // (TC, NW, 2N) fp32
-  static constexpr int RED = Gm::TC * Gm::NW * 2 * N * 4;
-  static constexpr int OFF_BAR = OFF_RED + RED;
+  static constexpr int ACT = TC * DT * (int)sizeof(T);
+  static constexpr int BC = TC * N * (int)sizeof(T);
+  static constexpr int OFF_U = 0, OFF_DT = ACT, OFF_Z = 2 * ACT, OFF_DY = 3 * ACT, OFF_YG = 4 * ACT,
+                       OFF_B = 5 * ACT, OFF_C = 5 * ACT + BC;
+  static constexpr int STAGE = 5 * ACT + 2 * BC;
+  // Tiles read or written in (step, channel) blocks of the lane layout use a padded row pitch
+  // that spreads such a block over the 32 banks (OP for T tiles, OPF for fp32 tiles).
+  static constexpr int OP = PadPitch<Gm::CPW, T>::value;
+  static constexpr int OPF = PadPitch<Gm::CPW, float>::value;
+  static constexpr int OUT = ((TC * OP * (int)sizeof(T)) + 127) / 128 * 128;
+  static constexpr int OFF_DYS = NSTAGE * STAGE;               // dy * silu(z), fp32, padded
+  static constexpr int OFF_BP = OFF_DYS + ((TC * OPF * 4 + 127) / 128) * 128;   // G perms x (16 x N) fp32 B
+  static constexpr int OFF_CP = OFF_BP + G * TC * N * 4;       // G perms x (16 x N) fp32 C
+  // Either the recomputed states (HSMEM) or the decays (ACACHE) are kept in shared memory;
+  // the other lives in registers / is recomputed.
+  static constexpr bool HSMEM = SSM_BWD_HSMEM != 0 && Gm::NT <= 256;
+  static constexpr bool ACACHE = !HSMEM && Gm::NT <= 256;
+  static constexpr int OFF_AC = OFF_CP + G * TC * N * 4;       // decay cache (TC x NT x G) fp32
+  static constexpr int OFF_OUT = OFF_AC + ((ACACHE || HSMEM) ? TC * Gm::NT * G * 4 : 0);   // NOUT x {du, ddelta, dz}
+  static constexpr int OFF_RED = OFF_OUT + NOUT * 3 * OUT;     // (TC, NW, 2N) fp32
+  static constexpr int OFF_DD = OFF_RED + TC * Gm::NW * 2 * N * 4;   // NT floats (dD partials)
+  static constexpr int OFF_BAR = OFF_DD + Gm::NT * 4;
   static constexpr int BYTES = OFF_BAR + NSTAGE * 8;
   static_assert(ACT % 128 == 0 && BC % 128 == 0, "TMA tiles must stay 128-byte aligned");
 };
 
-template <int N, typename T>
+template <typename S>
 __device__ __forceinline__ void bwd_issue_loads(const BwdParams& p, unsigned char* st, uint64_t* bar, int d0,
                                                 int t0, int b) {
-  using S = BwdSmem<N, T>;
-  const uint32_t tx = 3 * S::ACT + 2 * S::BC + (p.has_z ? S::ACT : 0);
+  const uint32_t tx = 3 * S::ACT + 2 * S::BC + (p.has_z ? 2 * S::ACT : 0);
   mbar_arrive_expect_tx(bar, tx);
   tma_load_3d(st + S::OFF_U, &p.tm_u, bar, d0, t0, b);
   tma_load_3d(st + S::OFF_DT, &p.tm_dt, bar, d0, t0, b);
   tma_load_3d(st + S::OFF_DY, &p.tm_dy, bar, d0, t0, b);
   tma_load_3d(st + S::OFF_B, &p.tm_B, bar, 0, t0, b);
   tma_load_3d(st + S::OFF_C, &p.tm_C, bar, 0, t0, b);
-  if (p.has_z) tma_load_3d(st + S::OFF_Z, &p.tm_z, bar, d0, t0, b);
+  if (p.has_z) {
+    tma_load_3d(st + S::OFF_Z, &p.tm_z, bar, d0, t0, b);
+    tma_load_3d(st + S::OFF_YG, &p.tm_yg, bar, d0, t0, b);
+  }
 }
 
-template <int N, typename T>
+template <typename S, int N, int NT, typename T>
 __device__ __forceinline__ void bwd_coop_load(const BwdParams& p, unsigned char* st, int d0, int t0, int b) {
-  using Gm = Geo<N>;
-  using S = BwdSmem<N, T>;
   const T zero = from_f32<T>(0.0f);
-  for (int e = threadIdx.x; e < Gm::TC * Gm::DT; e += Gm::NT) {
-    const int tt = e / Gm::DT, dd = e % Gm::DT;
+  for (int e = threadIdx.x; e < S::TC * S::DT; e += NT) {
+    const int tt = e / S::DT, dd = e % S::DT;
     const int t = t0 + tt, dg = d0 + dd;
     const bool ok = t < p.L && dg < p.D;
     const long long tl = t;
-    reinterpret_cast<T*>(st + S::OFF_U)[e] =
-        ok ? static_cast<const T*>(p.u.ptr)[b * p.u.sb + tl * p.u.sl + dg] : zero;
-    reinterpret_cast<T*>(st + S::OFF_DT)[e] =
-        ok ? static_cast<const T*>(p.dt.ptr)[b * p.dt.sb + tl * p.dt.sl + dg] : zero;
-    reinterpret_cast<T*>(st + S::OFF_DY)[e] =
-        ok ? static_cast<const T*>(p.dy.ptr)[b * p.dy.sb + tl * p.dy.sl + dg] : zero;
-    if (p.has_z)
-      reinterpret_cast<T*>(st + S::OFF_Z)[e] =
-          ok ? static_cast<const T*>(p.z.ptr)[b * p.z.sb + tl * p.z.sl + dg] : zero;
+    auto ld = [&](const DAct& a) { return ok ? static_cast<const T*>(a.ptr)[b * a.sb + tl * a.sl + dg] : zero; };
+    reinterpret_cast<T*>(st + S::OFF_U)[e] = ld(p.u);
+    reinterpret_cast<T*>(st + S::OFF_DT)[e] = ld(p.dt);
+    reinterpret_cast<T*>(st + S::OFF_DY)[e] = ld(p.dy);
+    if (p.has_z) {
+      reinterpret_cast<T*>(st + S::OFF_Z)[e] = ld(p.z);
+      reinterpret_cast<T*>(st + S::OFF_YG)[e] = ld(p.yg);
+    }
   }
-  for (int e = threadIdx.x; e < Gm::TC * N; e += Gm::NT) {
+  for (int e = threadIdx.x; e < S::TC * N; e += NT) {
     const int tt = e / N, n = e % N;
     const int t = t0 + tt;
     const bool ok = t < p.L;
@@ -94,20 +119,33 @@ __device__ __forceinline__ void bwd_coop_load(const BwdParams& p, unsigned char*
   }
 }
 
-template <int N, int METHOD, typename T>
-__global__ void __launch_bounds__(Geo<N>::NT) ssm_bwd_kernel(const __grid_constant__ BwdParams p) {
-  using Gm = Geo<N>;
-  using S = BwdSmem<N, T>;
-  constexpr int TC = Gm::TC, DT = Gm::DT, LPC = Gm::LPC, CPW = Gm::CPW, NW = Gm::NW;
-  constexpr int TG = (LPC <= 4) ? LPC : 1;          // time steps per (y, du, ddelta) reduction
-  constexpr int RV = 4 * TG;                         // values per reduction (y, du, ddelta, pad)
-  constexpr int VPL = (8 >= CPW) ? 8 / CPW : 1;      // dB|dC values per lane after transposition
-  constexpr int DUP = (CPW > 8) ? CPW / 8 : 1;       // lanes holding the same dB|dC value
+constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v / 2); }
+
+// G = 2 exists to raise occupancy, so its register budget is capped at two CTAs per SM.
+template <int N, int G, int METHOD, typename T>
+__global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kernel(const __grid_constant__ BwdParams p) {
+  using Gm = Geo<N, G>;
+  using S = BwdSmem<N, G, T>;
+  constexpr int TC = Gm::TC, DT = Gm::DT, LPC = Gm::LPC, CPW = Gm::CPW, NW = Gm::NW, NT = Gm::NT;
+  constexpr int OP = S::OP, OPF = S::OPF;
+  constexpr int LC = ilog2(CPW), LG = ilog2(G);
+  constexpr int NSLOT = LC < LG ? LC : LG;             // slot-splitting stages (select-free)
+  constexpr int KF = G >> NSLOT;                       // live slots after them
+  constexpr bool QSTAGE = LC > LG;                     // a dB / dC splitting stage follows
+  constexpr int BCPL = QSTAGE ? 1 : 2 * KF;            // dB|dC values per lane at the end
+  constexpr int BCDUP = (LC > LG + 1) ? (1 << (LC - LG - 1)) : 1;
+  // (du, ddelta) over the LPC lanes of a channel, 4 steps per transposition: V = 8 values
+  constexpr int QV = 8;
+  constexpr int QPL = (QV >= LPC) ? QV / LPC : 1;      // values per lane afterwards
+  constexpr int QDUP = (LPC > QV) ? LPC / QV : 1;      // lanes holding the same value
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
-  float* SDYS = reinterpret_cast<float*>(smem + S::OFF_DYS);
-  float* SSIG = reinterpret_cast<float*>(smem + S::OFF_SIG);
-  float* SRED = reinterpret_cast<float*>(smem + S::OFF_RED);
+  float* __restrict__ SDYS = reinterpret_cast<float*>(smem + S::OFF_DYS);
+  float* __restrict__ SBP = reinterpret_cast<float*>(smem + S::OFF_BP);
+  float* __restrict__ SCP = reinterpret_cast<float*>(smem + S::OFF_CP);
+  float* __restrict__ SAC = reinterpret_cast<float*>(smem + S::OFF_AC);
+  float* __restrict__ SRED = reinterpret_cast<float*>(smem + S::OFF_RED);
+  float* __restrict__ SDD = reinterpret_cast<float*>(smem + S::OFF_DD);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = lane / LPC, g = lane % LPC;
@@ -116,24 +154,29 @@ __global__ void __launch_bounds__(Geo<N>::NT) ssm_bwd_kernel(const __grid_consta
   const int d0 = dtile * DT, d = d0 + dl;
   const bool dvalid = d < p.D;
   const int nch = p.nchunks;
-
-  float Ak[4], A2[4], iA[4];
-  {
-    float a4[4] = {-1.f, -1.f, -1.f, -1.f};
-    if (dvalid) load4(p.A + (size_t)d * N + g * 4, a4);
+  const int nbase = g * G;
+  // register slot j holds state nbase + (j ^ perm); slot bit (LG-1-s) = c bit (LC-1-s)
+  int perm = 0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      Ak[k] = a4[k];
-      A2[k] = a4[k] * kLog2e;
-      iA[k] = 1.0f / a4[k];
-    }
+  for (int s2 = 0; s2 < NSLOT; ++s2) perm |= ((c >> (LC - 1 - s2)) & 1) << (LG - 1 - s2);
+
+  float Ak[G], A2[G], iA[G];
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const float a = dvalid ? p.A[(size_t)d * N + nbase + (j ^ perm)] : -1.f;
+    Ak[j] = a;
+    A2[j] = a * kLog2e;
+    iA[j] = 1.0f / a;
   }
   const float Dd = (p.Dskip != nullptr && dvalid) ? p.Dskip[d] : 0.0f;
-  const size_t bd = ((size_t)b * p.D + d) * N + g * 4;
+  const size_t bd = ((size_t)b * p.D + d) * N + nbase;
 
-  float dh[4] = {0.f, 0.f, 0.f, 0.f};
-  if (dvalid && p.dlast != nullptr) load4(p.dlast + bd, dh);
-  float dAA[4] = {0.f, 0.f, 0.f, 0.f};
+  float dh[G], dAA[G];
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    dh[j] = (dvalid && p.dlast != nullptr) ? p.dlast[bd + (j ^ perm)] : 0.f;
+    dAA[j] = 0.f;
+  }
   float dDacc = 0.0f;
 
   if (p.use_tma) {
@@ -145,189 +188,265 @@ __global__ void __launch_bounds__(Geo<N>::NT) ssm_bwd_kernel(const __grid_consta
     __syncthreads();
     if (tid == 0) {
       for (int s = 0; s < S::NSTAGE && s < nch; ++s)
-        bwd_issue_loads<N, T>(p, smem + s * S::STAGE, &bars[s], d0, (nch - 1 - s) * TC, b);
+        bwd_issue_loads<S>(p, smem + s * S::STAGE, &bars[s], d0, (nch - 1 - s) * TC, b);
     }
   }
 
-  auto cs_ptr = [&](int ch) { return p.chunk_states + (((size_t)b * nch + ch) * p.D + d) * N + g * 4; };
-  float hs[4] = {0.f, 0.f, 0.f, 0.f};
-  if (dvalid) load4(cs_ptr(nch - 1), hs);
+  auto load_state = [&](int ch, float (&o)[G]) {
+    const float* src = p.chunk_states + (((size_t)b * nch + ch) * p.D + d) * N + nbase;
+#pragma unroll
+    for (int j = 0; j < G; ++j) o[j] = dvalid ? src[j ^ perm] : 0.f;
+  };
+  float hs[G];
+  load_state(nch - 1, hs);
 
   for (int i = 0; i < nch; ++i) {
     const int ch = nch - 1 - i;
     const int s = i % S::NSTAGE;
     const int t0 = ch * TC;
     unsigned char* st = smem + s * S::STAGE;
-    float hs_next[4] = {0.f, 0.f, 0.f, 0.f};
-    if (dvalid && ch > 0) load4(cs_ptr(ch - 1), hs_next);
+    float hs_next[G];
+    if (ch > 0) {
+      load_state(ch - 1, hs_next);
+    } else {
+#pragma unroll
+      for (int j = 0; j < G; ++j) hs_next[j] = 0.f;
+    }
 
     if (p.use_tma) {
       mbar_wait(&bars[s], (uint32_t)((i / S::NSTAGE) & 1), p.err);
     } else {
-      bwd_coop_load<N, T>(p, st, d0, t0, b);
+      bwd_coop_load<S, N, NT, T>(p, st, d0, t0, b);
       __syncthreads();
     }
-    const T* Xs = reinterpret_cast<const T*>(st + S::OFF_U);
-    const T* DLs = reinterpret_cast<const T*>(st + S::OFF_DT);
-    const T* Zs = reinterpret_cast<const T*>(st + S::OFF_Z);
-    const T* DYs = reinterpret_cast<const T*>(st + S::OFF_DY);
-    const T* Bs = reinterpret_cast<const T*>(st + S::OFF_B);
-    const T* Cs = reinterpret_cast<const T*>(st + S::OFF_C);
+    const T* __restrict__ Xs = reinterpret_cast<const T*>(st + S::OFF_U);
+    const T* __restrict__ DLs = reinterpret_cast<const T*>(st + S::OFF_DT);
+    T* DUo = reinterpret_cast<T*>(smem + S::OFF_OUT + (i % S::NOUT) * 3 * S::OUT);
+    T* DDTo = reinterpret_cast<T*>(smem + S::OFF_OUT + (i % S::NOUT) * 3 * S::OUT + S::OUT);
+    T* DZo = reinterpret_cast<T*>(smem + S::OFF_OUT + (i % S::NOUT) * 3 * S::OUT + 2 * S::OUT);
 
-    // Gate terms once per (t, d):  dys = dy * silu(z)  (the scan's output gradient)
-    for (int e = tid; e < TC * DT; e += Gm::NT) {
-      const float dyv = to_f32(DYs[e]);
-      if (p.has_z) {
-        const float zz = to_f32(Zs[e]);
-        const float sg = sigmoid(zz);
-        SSIG[e] = sg;
-        SDYS[e] = dyv * zz * sg;
-      } else {
-        SDYS[e] = dyv;
+    // (2) gate pass over (t, d), and the state-permuted fp32 copies of B and C
+    {
+      const T* Zs = reinterpret_cast<const T*>(st + S::OFF_Z);
+      const T* DYs = reinterpret_cast<const T*>(st + S::OFF_DY);
+      const T* YGs = reinterpret_cast<const T*>(st + S::OFF_YG);
+      for (int e = tid; e < TC * DT; e += NT) {
+        const int ep = (e / DT) * OP + (e % DT), epf = (e / DT) * OPF + (e % DT);
+        const float dyv = to_f32(DYs[e]);
+        const float uu = to_f32(Xs[e]);
+        float dys = dyv;
+        if (p.has_z) {
+          const float zz = to_f32(Zs[e]);
+          const float sg = sigmoid(zz);
+          dys = dyv * zz * sg;
+          DZo[ep] = from_f32<T>(dyv * to_f32(YGs[e]) * sg * fmaf(zz, 1.0f - sg, 1.0f));
+        }
+        SDYS[epf] = dys;
+        dDacc = fmaf(dys, uu, dDacc);   // thread tid always sees channel tid % 32
+      }
+      const T* Bs = reinterpret_cast<const T*>(st + S::OFF_B);
+      const T* Cs = reinterpret_cast<const T*>(st + S::OFF_C);
+      for (int e = tid; e < G * TC * N; e += NT) {
+        const int pm = e / (TC * N), r = e % (TC * N);
+        const int n = r % N, src = (r - n) + ((n & ~(G - 1)) | ((n & (G - 1)) ^ pm));
+        SBP[e] = to_f32(Bs[src]);
+        SCP[e] = to_f32(Cs[src]);
       }
     }
     __syncthreads();
+    const float* __restrict__ Bp = SBP + perm * TC * N + nbase;
+    const float* __restrict__ Cp = SCP + perm * TC * N + nbase;
+    float* __restrict__ Acache = SAC + tid * G;
 
-    // (2) recompute the chunk's states from its checkpoint
-    float H[TC][4];
+    // (3) recompute the chunk's states from its checkpoint; cache the decays (or the states)
+    float H[S::HSMEM ? 1 : TC][G];
     {
-      float hc[4] = {hs[0], hs[1], hs[2], hs[3]};
+      float hc[G];
+#pragma unroll
+      for (int k = 0; k < G; ++k) hc[k] = hs[k];
 #pragma unroll
       for (int j = 0; j < TC; ++j) {
         const float uu = to_f32(Xs[j * DT + dl]);
         const float dtv = to_f32(DLs[j * DT + dl]);
         const float dtu = dtv * uu;
-        float Bn[4];
-        load4(Bs + j * N + g * 4, Bn);
+        float Bn[G], av[G];
+        loadg<G>(Bp + j * N, Bn);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < G; ++k) {
           if (METHOD == kZOH) {
             const float a = ex2(dtv * A2[k]);
             const float gg = (Bn[k] * uu) * iA[k];
             hc[k] = fmaf(a, hc[k] + gg, -gg);
+            av[k] = a;
           } else if (METHOD == kEuler) {
-            hc[k] = fmaf(ex2(dtv * A2[k]), hc[k], dtu * Bn[k]);
+            const float a = ex2(dtv * A2[k]);
+            hc[k] = fmaf(a, hc[k], dtu * Bn[k]);
+            av[k] = a;
           } else {
             const float zz = dtv * Ak[k];
             const float w = rcp(fmaf(-0.5f, zz, 1.0f));
             hc[k] = fmaf(fmaf(0.5f, zz, 1.0f) * w, hc[k], (dtu * Bn[k]) * w);
+            av[k] = w;   // bilinear caches w = 1/(1 - z/2); a = (1 + z/2) w
           }
-          H[j][k] = hc[k];
+          if (!S::HSMEM) H[S::HSMEM ? 0 : j][k] = hc[k];
         }
+        if (S::ACACHE) storeg<G>(Acache + j * NT * G, av);
+        if (S::HSMEM) storeg<G>(Acache + j * NT * G, hc);
       }
     }
 
-    // (3) reverse adjoint through the chunk
-    T* DUo = reinterpret_cast<T*>(smem + S::OFF_OUT + (i % S::NOUT) * 3 * S::ACT);
-    T* DDTo = DUo + TC * DT;
-    T* DZo = DDTo + TC * DT;
+    // (4) reverse adjoint through the chunk
+    float keep_q[TC / 4][QPL];   // (du, ddelta) results, 4 steps per group
+    float keep_bc[TC][BCPL];     // dB | dC results, per step
+    float hnext[G];              // HSMEM: state of step j, carried from step j + 1's load
+    if (S::HSMEM) loadg<G>(Acache + (TC - 1) * NT * G, hnext);
 #pragma unroll
-    for (int jg = TC / TG - 1; jg >= 0; --jg) {
-      float red[RV];
+    for (int jg = TC / 4 - 1; jg >= 0; --jg) {
+      float red[QV];
 #pragma unroll
-      for (int jj = TG - 1; jj >= 0; --jj) {
-        const int j = jg * TG + jj;
+      for (int jj = 3; jj >= 0; --jj) {
+        const int j = jg * 4 + jj;
         const float uu = to_f32(Xs[j * DT + dl]);
         const float dtv = to_f32(DLs[j * DT + dl]);
-        const float dys = SDYS[j * DT + dl];
-        float Bn[4], Cn[4];
-        load4(Bs + j * N + g * 4, Bn);
-        load4(Cs + j * N + g * 4, Cn);
-        float yv = 0.f, duv = 0.f, ddtv = 0.f;
-        float bc[8];
+        const float dys = SDYS[j * OPF + dl];
+        float Bn[G], Cn[G], av[G];
+        loadg<G>(Bp + j * N, Bn);
+        loadg<G>(Cp + j * N, Cn);
+        if (S::ACACHE) {
+          loadg<G>(Acache + j * NT * G, av);
+        } else {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float ht = H[j][k];
-          const float hp = (j > 0) ? H[j > 0 ? j - 1 : 0][k] : hs[k];
+          for (int k = 0; k < G; ++k)
+            av[k] = (METHOD == kBilinear) ? rcp(fmaf(-0.5f * dtv, Ak[k], 1.0f)) : ex2(dtv * A2[k]);
+        }
+        float duv = 0.f, ddtv = 0.f;
+        float bB[G], bC[G];
+        float hprev[G];
+        if (S::HSMEM) {
+          if (j > 0) {
+            loadg<G>(Acache + (j > 0 ? j - 1 : 0) * NT * G, hprev);
+          } else {
+#pragma unroll
+            for (int k = 0; k < G; ++k) hprev[k] = hs[k];
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < G; ++k) {
+          const float ht = S::HSMEM ? hnext[k] : H[S::HSMEM ? 0 : j][k];
+          const float hp = S::HSMEM ? hprev[k] : ((j > 0) ? H[(S::HSMEM || j == 0) ? 0 : j - 1][k] : hs[k]);
           const float Bu = Bn[k] * uu;
           dh[k] = fmaf(dys, Cn[k], dh[k]);
-          bc[4 + k] = dys * ht;
-          yv = fmaf(Cn[k], ht, yv);
+          bC[k] = dys * ht;
           if (METHOD == kZOH) {
-            const float a = ex2(dtv * A2[k]);
-            const float q = dh[k] * a;
+            const float q = dh[k] * av[k];
             const float sv = q * fmaf(Ak[k], hp, Bu);
             ddtv += sv;
             const float pp = (q - dh[k]) * iA[k];
             duv = fmaf(pp, Bn[k], duv);
-            bc[k] = pp * uu;
+            bB[k] = pp * uu;
             dAA[k] = fmaf(dtv, sv, dAA[k]);
             dAA[k] = fmaf(-pp, Bu, dAA[k]);
             dh[k] = q;
           } else if (METHOD == kEuler) {
-            const float a = ex2(dtv * A2[k]);
-            const float q = dh[k] * a;
+            const float q = dh[k] * av[k];
             const float sv = fmaf(q * Ak[k], hp, dh[k] * Bu);
             ddtv += sv;
             const float pp = dh[k] * dtv;
             duv = fmaf(pp, Bn[k], duv);
-            bc[k] = pp * uu;
+            bB[k] = pp * uu;
             dAA[k] = fmaf(dtv * q, hp, dAA[k]);
             dh[k] = q;
           } else {
+            const float w = av[k];
             const float zz = dtv * Ak[k];
-            const float w = rcp(fmaf(-0.5f, zz, 1.0f));
             const float a = fmaf(0.5f, zz, 1.0f) * w;
             const float dhw2 = dh[k] * w * w;
             const float sv = dhw2 * fmaf(Ak[k], hp, Bu);
             ddtv += sv;
             const float pp = dh[k] * dtv * w;
             duv = fmaf(pp, Bn[k], duv);
-            bc[k] = pp * uu;
+            bB[k] = pp * uu;
             dAA[k] = fmaf(dtv * dhw2, fmaf(0.5f * dtv, Bu, hp), dAA[k]);
             dh[k] = dh[k] * a;
           }
         }
-        // dB | dC: sum over this warp's channels, then park per (t, warp) for the cross-warp sum
-        xpose_reduce<8, CPW, LPC>(bc, lane);
-        if (c % DUP == 0) {
+        // dB | dC over the warp's channels: slot-splitting stages first (a fixed register
+        // slot is sent on every lane thanks to the state permutation), then one stage that
+        // splits dB from dC, then all-reduce stages for the remaining channel bits.
 #pragma unroll
-          for (int v = 0; v < VPL; ++v) {
-            const int idx = (c / DUP) * VPL + v;   // quantity: (idx >> 2) = 0 dB / 1 dC, state g*4 + (idx & 3)
-            SRED[(j * NW + warp) * 2 * N + (idx >> 2) * N + g * 4 + (idx & 3)] = bc[v];
+        for (int s2 = 0; s2 < NSLOT; ++s2) {
+          const int m = (CPW >> (s2 + 1)) * LPC;
+          const int half = G >> (s2 + 1);
+#pragma unroll
+          for (int k = 0; k < half; ++k) {
+            bB[k] += __shfl_xor_sync(0xffffffffu, bB[k + half], m);
+            bC[k] += __shfl_xor_sync(0xffffffffu, bC[k + half], m);
           }
         }
-        red[jj * 4 + 0] = yv;
-        red[jj * 4 + 1] = duv;
-        red[jj * 4 + 2] = ddtv;
-        red[jj * 4 + 3] = 0.f;
-      }
-      // (y, du, ddelta) over the LPC lanes of the channel
-      float yv, duv, ddtv;
-      int j;
-      if (TG == LPC) {
-        xpose_reduce<RV, LPC, 1>(red, lane);  // lane g: timestep jg*TG + g
-        yv = red[0]; duv = red[1]; ddtv = red[2];
-        j = jg * TG + g;
-      } else {                                 // TG == 1, LPC > 4
-        yv = group_allreduce<LPC, 1>(red[0]);
-        duv = group_allreduce<LPC, 1>(red[1]);
-        ddtv = group_allreduce<LPC, 1>(red[2]);
-        j = jg;
-      }
-      if (TG == LPC || g == 0) {
-        const float uu = to_f32(Xs[j * DT + dl]);
-        const float dys = SDYS[j * DT + dl];
-        DUo[j * DT + dl] = from_f32<T>(duv + Dd * dys);
-        DDTo[j * DT + dl] = from_f32<T>(ddtv);
-        if (p.has_z) {
-          const float zz = to_f32(Zs[j * DT + dl]);
-          const float sg = SSIG[j * DT + dl];
-          const float dyv = to_f32(DYs[j * DT + dl]);
-          const float yfull = fmaf(Dd, uu, yv);
-          DZo[j * DT + dl] = from_f32<T>(dyv * yfull * sg * fmaf(zz, 1.0f - sg, 1.0f));
+        if constexpr (QSTAGE) {
+          constexpr int m = (CPW >> (LG + 1)) * LPC;
+          const bool up = (c >> (LC - LG - 1)) & 1;
+          const float send = up ? bB[0] : bC[0];
+          float kv = (up ? bC[0] : bB[0]) + __shfl_xor_sync(0xffffffffu, send, m);
+#pragma unroll
+          for (int mm = CPW >> (LG + 2); mm >= 1; mm >>= 1) kv += __shfl_xor_sync(0xffffffffu, kv, mm * LPC);
+          keep_bc[j][0] = kv;
+        } else {
+#pragma unroll
+          for (int k = 0; k < KF; ++k) {
+            keep_bc[j][k] = bB[k];
+            keep_bc[j][(KF + k) % BCPL] = bC[k];
+          }
         }
-        dDacc = fmaf(dys, uu, dDacc);
+        red[jj * 2 + 0] = duv;
+        red[jj * 2 + 1] = ddtv;
+        if (S::HSMEM) {
+#pragma unroll
+          for (int k = 0; k < G; ++k) hnext[k] = hprev[k];
+        }
+      }
+      xpose_reduce<QV, LPC, 1>(red, lane);
+#pragma unroll
+      for (int v = 0; v < QPL; ++v) keep_q[jg][v] = red[v];
+    }
+
+    // chunk epilogue: dB|dC per (step, warp) into shared memory, du / ddelta tiles
+#pragma unroll
+    for (int j = 0; j < TC; ++j) {
+      float* dst = SRED + (j * NW + warp) * 2 * N;
+      if constexpr (QSTAGE) {
+        if ((c & (BCDUP - 1)) == 0) {
+          const int q = (c >> (LC - LG - 1)) & 1;
+          dst[q * N + nbase + perm] = keep_bc[j][0];
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < KF; ++k) {
+          dst[nbase + (k ^ perm)] = keep_bc[j][k];
+          dst[N + nbase + (k ^ perm)] = keep_bc[j][(KF + k) % BCPL];
+        }
+      }
+    }
+    if ((g % QDUP) == 0) {
+#pragma unroll
+      for (int jg = 0; jg < TC / 4; ++jg) {
+#pragma unroll
+        for (int v = 0; v < QPL; ++v) {
+          const int idx = (g / QDUP) * QPL + v;   // value index: step jg*4 + idx/2, quantity idx%2
+          const int j = jg * 4 + (idx >> 1);
+          if (idx & 1) {
+            DDTo[j * OP + dl] = from_f32<T>(keep_q[jg][v]);
+          } else {
+            DUo[j * OP + dl] = from_f32<T>(fmaf(Dd, SDYS[j * OPF + dl], keep_q[jg][v]));
+          }
+        }
       }
     }
 
-    if (p.use_tma) {
-      fence_proxy_async_smem();
-    }
     __syncthreads();
 
     // cross-warp dB | dC sum -> this CTA's partial (fixed order)
-    for (int e = tid; e < TC * 2 * N; e += Gm::NT) {
+    for (int e = tid; e < TC * 2 * N; e += NT) {
       const int j = e / (2 * N), v = e % (2 * N);
       float sum = 0.f;
 #pragma unroll
@@ -336,43 +455,31 @@ __global__ void __launch_bounds__(Geo<N>::NT) ssm_bwd_kernel(const __grid_consta
       if (t < p.L) p.part_bc[(((size_t)b * p.ndt + dtile) * p.L + t) * 2 * N + v] = sum;
     }
 
-    if (p.use_tma) {
-      if (tid == 0) {
-        tma_store_3d(&p.tm_du, DUo, d0, t0, b);
-        tma_store_3d(&p.tm_ddt, DDTo, d0, t0, b);
-        if (p.has_z) tma_store_3d(&p.tm_dz, DZo, d0, t0, b);
-        tma_store_commit();
-        if (ch - S::NSTAGE >= 0) bwd_issue_loads<N, T>(p, st, &bars[s], d0, (ch - S::NSTAGE) * TC, b);
-        // the output buffer written next chunk was last read by the store issued one chunk ago
-        tma_store_wait_read<1>();
-      }
-    } else {
-      for (int e = tid; e < TC * DT; e += Gm::NT) {
-        const int tt = e / DT, dd = e % DT;
-        const int t = t0 + tt, dg = d0 + dd;
-        if (t < p.L && dg < p.D) {
-          const long long tl = t;
-          static_cast<T*>(const_cast<void*>(p.du.ptr))[b * p.du.sb + tl * p.du.sl + dg] = DUo[e];
-          static_cast<T*>(const_cast<void*>(p.ddt.ptr))[b * p.ddt.sb + tl * p.ddt.sl + dg] = DDTo[e];
-          if (p.has_z) static_cast<T*>(const_cast<void*>(p.dz.ptr))[b * p.dz.sb + tl * p.dz.sl + dg] = DZo[e];
-        }
-      }
-    }
+    if (p.use_tma && tid == 0 && ch - S::NSTAGE >= 0)
+      bwd_issue_loads<S>(p, st, &bars[s], d0, (ch - S::NSTAGE) * TC, b);
+    store_tile<NT, OP>(DUo, p.du, b, t0, d0, p.L, p.D);
+    store_tile<NT, OP>(DDTo, p.ddt, b, t0, d0, p.L, p.D);
+    if (p.has_z) store_tile<NT, OP>(DZo, p.dz, b, t0, d0, p.L, p.D);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) hs[k] = hs_next[k];
+    for (int k = 0; k < G; ++k) hs[k] = hs_next[k];
   }
 
   // per-(b, d) partials; ssm_bwd_finalize sums them over b in fixed order
-  dDacc = group_allreduce<LPC, 1>(dDacc);
+  SDD[tid] = dDacc;
+  __syncthreads();
   if (dvalid) {
-    float o[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) o[k] = (METHOD == kZOH) ? dAA[k] * iA[k] : dAA[k];
-    *reinterpret_cast<float4*>(p.part_A + bd) = make_float4(o[0], o[1], o[2], o[3]);
-    if (p.dh0 != nullptr) *reinterpret_cast<float4*>(p.dh0 + bd) = make_float4(dh[0], dh[1], dh[2], dh[3]);
-    if (g == 0) p.part_D[(size_t)b * p.D + d] = dDacc;
+    for (int j = 0; j < G; ++j) {
+      const size_t o = bd + (j ^ perm);
+      p.part_A[o] = (METHOD == kZOH) ? dAA[j] * iA[j] : dAA[j];
+      if (p.dh0 != nullptr) p.dh0[o] = dh[j];
+    }
   }
-  if (p.use_tma && tid == 0) tma_store_wait_all<0>();
+  if (tid < DT && d0 + tid < p.D) {
+    float sdd = 0.f;
+    for (int w = 0; w < NT / DT; ++w) sdd += SDD[w * DT + tid];
+    p.part_D[(size_t)b * p.D + d0 + tid] = sdd;
+  }
 }
 
 // Sums the per-CTA dB | dC partials over channel tiles and the dA / dD partials over batch,
@@ -412,7 +519,7 @@ __global__ void ssm_bwd_finalize(const FinParams p) {
 }
 
 template <typename T>
-cudaError_t launch_bwd(int N, int method, const BwdParams& p, dim3 grid, cudaStream_t stream);
+cudaError_t launch_bwd(int N, int G, int method, const BwdParams& p, dim3 grid, cudaStream_t stream);
 template <typename T>
 cudaError_t launch_bwd_finalize(const FinParams& p, cudaStream_t stream);
 

@@ -5,36 +5,44 @@
 
 namespace ssm {
 
-template <typename T, int N, int METHOD>
+template <typename T, int N, int G, int METHOD>
 static cudaError_t launch_bwd_nm(const BwdParams& p, dim3 grid, cudaStream_t stream) {
-  auto kern = ssm_bwd_kernel<N, METHOD, T>;
-  constexpr int smem = BwdSmem<N, T>::BYTES;
+  auto kern = ssm_bwd_kernel<N, G, METHOD, T>;
+  constexpr int smem = BwdSmem<N, G, T>::BYTES;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
   }
-  kern<<<grid, Geo<N>::NT, smem, stream>>>(p);
+  kern<<<grid, Geo<N, G>::NT, smem, stream>>>(p);
   return cudaGetLastError();
 }
 
-template <typename T, int N>
+template <typename T, int N, int G>
 static cudaError_t launch_bwd_n(int method, const BwdParams& p, dim3 grid, cudaStream_t stream) {
   switch (method) {
-    case kZOH: return launch_bwd_nm<T, N, kZOH>(p, grid, stream);
-    case kEuler: return launch_bwd_nm<T, N, kEuler>(p, grid, stream);
-    case kBilinear: return launch_bwd_nm<T, N, kBilinear>(p, grid, stream);
+    case kZOH: return launch_bwd_nm<T, N, G, kZOH>(p, grid, stream);
+    case kEuler: return launch_bwd_nm<T, N, G, kEuler>(p, grid, stream);
+    case kBilinear: return launch_bwd_nm<T, N, G, kBilinear>(p, grid, stream);
   }
   return cudaErrorInvalidValue;
 }
 
+// G = 2 (twice the threads for small grids) is built for N = 8 and 16.
 template <>
-cudaError_t launch_bwd<SSM_ELEM>(int N, int method, const BwdParams& p, dim3 grid, cudaStream_t stream) {
+cudaError_t launch_bwd<SSM_ELEM>(int N, int G, int method, const BwdParams& p, dim3 grid, cudaStream_t stream) {
+  if (G == 2) {
+    switch (N) {
+      case 8: return launch_bwd_n<SSM_ELEM, 8, 2>(method, p, grid, stream);
+      case 16: return launch_bwd_n<SSM_ELEM, 16, 2>(method, p, grid, stream);
+    }
+    return cudaErrorInvalidValue;
+  }
   switch (N) {
-    case 4: return launch_bwd_n<SSM_ELEM, 4>(method, p, grid, stream);
-    case 8: return launch_bwd_n<SSM_ELEM, 8>(method, p, grid, stream);
-    case 16: return launch_bwd_n<SSM_ELEM, 16>(method, p, grid, stream);
-    case 32: return launch_bwd_n<SSM_ELEM, 32>(method, p, grid, stream);
-    case 64: return launch_bwd_n<SSM_ELEM, 64>(method, p, grid, stream);
+    case 4: return launch_bwd_n<SSM_ELEM, 4, 4>(method, p, grid, stream);
+    case 8: return launch_bwd_n<SSM_ELEM, 8, 4>(method, p, grid, stream);
+    case 16: return launch_bwd_n<SSM_ELEM, 16, 4>(method, p, grid, stream);
+    case 32: return launch_bwd_n<SSM_ELEM, 32, 4>(method, p, grid, stream);
+    case 64: return launch_bwd_n<SSM_ELEM, 64, 4>(method, p, grid, stream);
   }
   return cudaErrorInvalidValue;
 }

@@ -1,9 +1,10 @@
 // ssm_common.cuh — device helpers and launch geometry shared by the selective-scan kernels.
 //
-// Geometry (all kernels): one thread owns 4 consecutive states (n = 4g .. 4g+3) of one
-// channel; N/4 consecutive lanes ("a channel group") cover all N states of a channel, so a
-// warp covers 128/N channels and a CTA of N/4 warps covers DT = 32 channels.  Time is
-// walked sequentially in tiles of TC = 16 steps that TMA stages into shared memory.
+// Geometry (all scan kernels): one thread owns G consecutive states (n = G g .. G g + G-1) of
+// one channel (G = 4, or G = 2 when the (batch x channel) grid is too small to fill the GPU);
+// N/G consecutive lanes ("a channel group") cover all N states of a channel, so a warp covers
+// 32 G / N channels and a CTA of N/G warps covers DT = 32 channels.  Time is walked
+// sequentially in tiles of TC = 16 steps that TMA stages into shared memory.
 #pragma once
 
 #include <cuda.h>
@@ -17,17 +18,17 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 enum { kZOH = 0, kEuler = 1, kBilinear = 2 };
 
-template <int N_>
+template <int N_, int G_ = 4>
 struct Geo {
   static constexpr int N = N_;
-  static constexpr int G = 4;              // states per thread
+  static constexpr int G = G_;             // states per thread
   static constexpr int LPC = N / G;        // lanes per channel
   static constexpr int CPW = 32 / LPC;     // channels per warp
   static constexpr int DT = 32;            // channels per CTA
-  static constexpr int NW = DT / CPW;      // warps per CTA (= N / 4)
-  static constexpr int NT = NW * 32;       // threads per CTA (= 8 N)
+  static constexpr int NW = DT / CPW;      // warps per CTA (= N / G)
+  static constexpr int NT = NW * 32;       // threads per CTA (= 32 N / G)
   static constexpr int TC = 16;            // time steps per tile (= checkpoint interval)
-  static_assert(N % G == 0 && LPC >= 1 && LPC <= 16, "N must be 4..64");
+  static_assert((G == 2 || G == 4) && N % G == 0 && LPC >= 1 && LPC <= 16, "unsupported N / G");
 };
 
 constexpr int kChunk = 16;  // checkpoint interval of chunk_states (time steps)
@@ -45,6 +46,25 @@ __device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&o)[4]) {
   const uint2 v = *reinterpret_cast<const uint2*>(p);
   o[0] = __uint_as_float(v.x << 16); o[1] = __uint_as_float(v.x & 0xffff0000u);
   o[2] = __uint_as_float(v.y << 16); o[3] = __uint_as_float(v.y & 0xffff0000u);
+}
+__device__ __forceinline__ void load2(const float* p, float (&o)[2]) {
+  const float2 v = *reinterpret_cast<const float2*>(p);
+  o[0] = v.x; o[1] = v.y;
+}
+__device__ __forceinline__ void load2(const __nv_bfloat16* p, float (&o)[2]) {
+  const uint32_t v = *reinterpret_cast<const uint32_t*>(p);
+  o[0] = __uint_as_float(v << 16); o[1] = __uint_as_float(v & 0xffff0000u);
+}
+// G consecutive values (G = 2 or 4) as float; p aligned to G elements.
+template <int G, typename T>
+__device__ __forceinline__ void loadg(const T* p, float (&o)[G]) {
+  if constexpr (G == 4) load4(p, o);
+  else load2(p, o);
+}
+template <int G>
+__device__ __forceinline__ void storeg(float* p, const float (&v)[G]) {
+  if constexpr (G == 4) *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  else *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
 }
 __device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
 template <typename T> __device__ __forceinline__ T from_f32(float x);
@@ -105,6 +125,47 @@ __device__ __forceinline__ float group_allreduce(float x) {
 #pragma unroll
   for (int m = GROUP / 2; m >= 1; m >>= 1) x += __shfl_xor_sync(0xffffffffu, x, m * STRIDE);
   return x;
+}
+
+struct DAct {                // (B, rows, cols) tensor with unit column stride
+  const void* ptr;
+  long long sb, sl;          // element strides of batch and row
+};
+
+// Row pitch (in elements of T) of a padded (16 x 32) shared tile written or read in blocks of
+// LPC rows x CPW consecutive channels: consecutive rows start SW 4-byte words apart, SW >= the
+// block's width in words and a multiple of 4, so rows stay 16-byte aligned (vector copies) and
+// a block spreads over the 32 banks (2-way overlap remains only for CPW = 2).
+template <int CPW, typename T>
+struct PadPitch {
+  static constexpr int WW = CPW * (int)sizeof(T) / 4 > 0 ? CPW * (int)sizeof(T) / 4 : 1;
+  static constexpr int SW = WW < 4 ? 4 : WW;
+  static constexpr int value = 32 + SW * 4 / (int)sizeof(T);
+  static_assert((value * (int)sizeof(T)) % 16 == 0, "padded rows must stay 16-byte aligned");
+};
+
+// Coalesced copy of a padded (16 x OP) shared tile to a (B, L, D) view (16-byte stores
+// where the row and view allow it).
+template <int NT, int OP, typename T>
+__device__ __forceinline__ void store_tile(const T* tile, const DAct& v, int b, int t0, int d0, int L, int D) {
+  constexpr int TC = 16, DT = 32, VEC = 16 / (int)sizeof(T);   // elements per 16 bytes
+  static_assert((OP * (int)sizeof(T)) % 16 == 0, "16-byte shared loads need 16-byte aligned rows");
+  T* base = static_cast<T*>(const_cast<void*>(v.ptr)) + b * v.sb;
+  const bool vec_ok = ((reinterpret_cast<uintptr_t>(base) | (uintptr_t)(v.sl * sizeof(T))) & 15) == 0 &&
+                      (d0 + DT <= D);
+  if (vec_ok) {
+    for (int e = threadIdx.x; e < TC * DT / VEC; e += NT) {
+      const int tt = e / (DT / VEC), q = e % (DT / VEC);
+      if (t0 + tt < L)
+        *reinterpret_cast<uint4*>(base + (long long)(t0 + tt) * v.sl + d0 + q * VEC) =
+            *reinterpret_cast<const uint4*>(tile + tt * OP + q * VEC);
+    }
+  } else {
+    for (int e = threadIdx.x; e < TC * DT; e += NT) {
+      const int tt = e / DT, dd = e % DT;
+      if (t0 + tt < L && d0 + dd < D) base[(long long)(t0 + tt) * v.sl + d0 + dd] = tile[tt * OP + dd];
+    }
+  }
 }
 
 // ------------------------------------------------------------------------------------------
@@ -173,14 +234,10 @@ __device__ __forceinline__ void tma_store_wait_all() {
 // ------------------------------------------------------------------------------------------
 // Kernel parameter blocks (passed as __grid_constant__ so the tensor maps stay addressable)
 // ------------------------------------------------------------------------------------------
-struct DAct {                // (B, rows, cols) tensor with unit column stride
-  const void* ptr;
-  long long sb, sl;          // element strides of batch and row
-};
 
 struct alignas(64) FwdParams {
-  CUtensorMap tm_u, tm_dt, tm_z, tm_B, tm_C, tm_y;
-  DAct u, dt, z, Bm, Cm, y;
+  CUtensorMap tm_u, tm_dt, tm_z, tm_B, tm_C;        // TMA loads (outputs use plain stores)
+  DAct u, dt, z, Bm, Cm, y, yg;   // yg: pre-gate output (y + Dskip u), written iff save_ygate
   const float* A;            // (D, N)
   const float* Dskip;        // (D) or null
   const float* h_init;       // (B, D, N) or null: state entering t = 0 (segment 0)
@@ -191,12 +248,12 @@ struct alignas(64) FwdParams {
   float* seg_decay;          // summary mode: (B, S, D, N)
   int* err;
   int B, L, D, nchunks, seg_len, nseg;
-  int has_z, use_tma;
+  int has_z, use_tma, save_ygate;
 };
 
 struct alignas(64) BwdParams {
-  CUtensorMap tm_u, tm_dt, tm_z, tm_dy, tm_B, tm_C, tm_du, tm_ddt, tm_dz;
-  DAct u, dt, z, dy, Bm, Cm, du, ddt, dz;
+  CUtensorMap tm_u, tm_dt, tm_z, tm_dy, tm_yg, tm_B, tm_C;   // TMA loads (outputs use plain stores)
+  DAct u, dt, z, dy, yg, Bm, Cm, du, ddt, dz;   // yg: the forward's pre-gate output (iff has_z)
   const float* A;
   const float* Dskip;
   const float* h0;           // (B, D, N) or null (only for dh0 presence)

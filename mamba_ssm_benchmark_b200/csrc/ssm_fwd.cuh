@@ -6,9 +6,10 @@
 //
 // One CTA owns a (batch, 32-channel tile, time segment).  The CTA walks its segment in tiles
 // of 16 steps; thread 0 streams u, delta, z (16 x 32) and B, C (16 x N) tiles through a
-// 3-stage TMA ring (mbarrier completion), every thread keeps its 4 states in registers, and
-// the gated output tile goes back to HBM with a TMA store.  The state entering every 16-step
-// chunk is written to chunk_states for the backward pass.
+// 3-stage TMA ring (mbarrier completion), every thread keeps its G states in registers, and
+// the gated output tile (and, for training, the pre-gate tile) goes back to HBM through a
+// bank-conflict-free padded shared tile and coalesced 16-byte stores.  The state entering every 16-step chunk is written to chunk_states for the
+// backward pass.
 //
 // Long sequences with few (batch, channel) tiles are split into S segments: a summary pass
 // (mode kModeSummary) scans every segment from a zero state and records its decay product
@@ -23,48 +24,57 @@ namespace ssm {
 
 enum { kModeMain = 0, kModeSummary = 1 };
 
-template <int N, typename T>
+template <int N, int G, typename T>
 struct FwdSmem {
-  using Gm = Geo<N>;
+  static constexpr int TC = 16, DT = 32;
   static constexpr int NSTAGE = 3;
-  static constexpr int NOUT = 3;
-  static constexpr int ACT = Gm::TC * Gm::DT * (int)sizeof(T);   // one (16 x 32) tile, bytes
-  static constexpr int BC = Gm::TC * N * (int)sizeof(T);          // one (16 x N) tile, bytes
+  static constexpr int NOUT = 2;
+  static constexpr int ACT = TC * DT * (int)sizeof(T);   // one dense (16 x 32) TMA tile, bytes
+  static constexpr int BC = TC * N * (int)sizeof(T);     // one (16 x N) tile, bytes
+  // Output tiles use a padded row pitch: the epilogue writes (step, channel) blocks of
+  // LPC rows x CPW channels, which the pitch spreads over the 32 banks.
+  static constexpr int OP = PadPitch<Geo<N, G>::CPW, T>::value;
+  static constexpr int OUT = ((TC * OP * (int)sizeof(T)) + 127) / 128 * 128;
   static constexpr int OFF_U = 0, OFF_DT = ACT, OFF_Z = 2 * ACT, OFF_B = 3 * ACT, OFF_C = 3 * ACT + BC;
   static constexpr int STAGE = 3 * ACT + 2 * BC;
-  static constexpr int OFF_Y = NSTAGE * STAGE;
-  static constexpr int OFF_BAR = OFF_Y + NOUT * ACT;
+  static constexpr int OFF_Y = NSTAGE * STAGE;             // NOUT x {y, pre-gate y}
+  static constexpr int OFF_BAR = OFF_Y + NOUT * 2 * OUT;
   static constexpr int BYTES = OFF_BAR + NSTAGE * 8;
   static_assert(ACT % 128 == 0 && BC % 128 == 0, "TMA tiles must stay 128-byte aligned");
 };
 
-// One time step of one state for the forward recurrence (discretize + update).
+// Discretization of one (step, state) split into the state-independent coefficients and the
+// update.  ZOH: b = expm1(dt A)/A B u is applied as h' = a (h + g) - g with g = B u / A, i.e.
+// the coefficient pair is (a, g); Euler and bilinear use h' = a h + b.
 template <int METHOD>
-__device__ __forceinline__ float fwd_step(float h, float dtv, float uu, float dtu, float Bn, float Ak, float A2,
-                                          float iA, float& a_out) {
+__device__ __forceinline__ void fwd_coeffs(float dtv, float uu, float dtu, float Bn, float Ak, float A2, float iA,
+                                           float& a, float& bcoef) {
   if (METHOD == kZOH) {
-    // b = expm1(dt A)/A * B u  ->  h' = a h + (a - 1) g  with g = B u / A  = a (h + g) - g
-    const float a = ex2(dtv * A2);
-    const float gg = (Bn * uu) * iA;
-    a_out = a;
-    return fmaf(a, h + gg, -gg);
+    a = ex2(dtv * A2);
+    bcoef = (Bn * uu) * iA;
   } else if (METHOD == kEuler) {
-    const float a = ex2(dtv * A2);
-    a_out = a;
-    return fmaf(a, h, dtu * Bn);
+    a = ex2(dtv * A2);
+    bcoef = dtu * Bn;
   } else {
     const float z = dtv * Ak;
     const float w = rcp(fmaf(-0.5f, z, 1.0f));
-    const float a = fmaf(0.5f, z, 1.0f) * w;
-    a_out = a;
-    return fmaf(a, h, (dtu * Bn) * w);
+    a = fmaf(0.5f, z, 1.0f) * w;
+    bcoef = (dtu * Bn) * w;
   }
 }
+template <int METHOD>
+__device__ __forceinline__ float fwd_apply(float h, float a, float bcoef) {
+  if (METHOD == kZOH) return fmaf(a, h + bcoef, -bcoef);
+  return fmaf(a, h, bcoef);
+}
 
-template <int N, typename T, int MODE>
+#ifndef SSM_FWD_SUB
+#define SSM_FWD_SUB 4   // steps per state-independent sub-tile (divides 16)
+#endif
+
+template <typename S, int MODE>
 __device__ __forceinline__ void fwd_issue_loads(const FwdParams& p, unsigned char* st, uint64_t* bar, int d0,
                                                 int t0, int b) {
-  using S = FwdSmem<N, T>;
   const bool load_zc = (MODE == kModeMain);
   const uint32_t tx = 2 * S::ACT + S::BC + (load_zc ? (S::BC + (p.has_z ? S::ACT : 0)) : 0);
   mbar_arrive_expect_tx(bar, tx);
@@ -78,25 +88,20 @@ __device__ __forceinline__ void fwd_issue_loads(const FwdParams& p, unsigned cha
 }
 
 // Cooperative (non-TMA) tile load with zero fill, for views TMA cannot describe.
-template <int N, typename T, int MODE>
+template <typename S, int N, int NT, typename T, int MODE>
 __device__ __forceinline__ void fwd_coop_load(const FwdParams& p, unsigned char* st, int d0, int t0, int b) {
-  using Gm = Geo<N>;
-  using S = FwdSmem<N, T>;
   const T zero = from_f32<T>(0.0f);
-  for (int e = threadIdx.x; e < Gm::TC * Gm::DT; e += Gm::NT) {
-    const int tt = e / Gm::DT, dd = e % Gm::DT;
+  for (int e = threadIdx.x; e < S::TC * S::DT; e += NT) {
+    const int tt = e / S::DT, dd = e % S::DT;
     const int t = t0 + tt, dg = d0 + dd;
     const bool ok = t < p.L && dg < p.D;
-    const T* u = static_cast<const T*>(p.u.ptr);
-    const T* dt = static_cast<const T*>(p.dt.ptr);
-    reinterpret_cast<T*>(st + S::OFF_U)[e] = ok ? u[b * p.u.sb + (long long)t * p.u.sl + dg] : zero;
-    reinterpret_cast<T*>(st + S::OFF_DT)[e] = ok ? dt[b * p.dt.sb + (long long)t * p.dt.sl + dg] : zero;
-    if (MODE == kModeMain && p.has_z) {
-      const T* z = static_cast<const T*>(p.z.ptr);
-      reinterpret_cast<T*>(st + S::OFF_Z)[e] = ok ? z[b * p.z.sb + (long long)t * p.z.sl + dg] : zero;
-    }
+    const long long tl = t;
+    auto ld = [&](const DAct& a) { return ok ? static_cast<const T*>(a.ptr)[b * a.sb + tl * a.sl + dg] : zero; };
+    reinterpret_cast<T*>(st + S::OFF_U)[e] = ld(p.u);
+    reinterpret_cast<T*>(st + S::OFF_DT)[e] = ld(p.dt);
+    if (MODE == kModeMain && p.has_z) reinterpret_cast<T*>(st + S::OFF_Z)[e] = ld(p.z);
   }
-  for (int e = threadIdx.x; e < Gm::TC * N; e += Gm::NT) {
+  for (int e = threadIdx.x; e < S::TC * N; e += NT) {
     const int tt = e / N, n = e % N;
     const int t = t0 + tt;
     const bool ok = t < p.L;
@@ -109,11 +114,12 @@ __device__ __forceinline__ void fwd_coop_load(const FwdParams& p, unsigned char*
   }
 }
 
-template <int N, int METHOD, typename T, int MODE>
-__global__ void __launch_bounds__(Geo<N>::NT) ssm_fwd_kernel(const __grid_constant__ FwdParams p) {
-  using Gm = Geo<N>;
-  using S = FwdSmem<N, T>;
-  constexpr int TC = Gm::TC, DT = Gm::DT, LPC = Gm::LPC, TG = LPC;
+template <int N, int G, int METHOD, typename T, int MODE>
+__global__ void __launch_bounds__(Geo<N, G>::NT) ssm_fwd_kernel(const __grid_constant__ FwdParams p) {
+  using Gm = Geo<N, G>;
+  using S = FwdSmem<N, G, T>;
+  constexpr int TC = Gm::TC, DT = Gm::DT, LPC = Gm::LPC, NT = Gm::NT, OP = S::OP;
+  constexpr int YPL = TC / LPC;   // output steps per lane after the y reduction
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
 
@@ -123,31 +129,39 @@ __global__ void __launch_bounds__(Geo<N>::NT) ssm_fwd_kernel(const __grid_consta
   const int b = blockIdx.z, seg = blockIdx.y;
   const int d0 = blockIdx.x * DT, d = d0 + dl;
   const bool dvalid = d < p.D;
+  const int nbase = g * G;
   const int t_begin = seg * p.seg_len;
   const int t_end = min(p.L, t_begin + p.seg_len);
   const int nblk = (t_end - t_begin + TC - 1) / TC;
 
   // Per-state constants: A, A log2(e) (for 2^x), 1/A.  Channels past D get A = -1, zero inputs.
-  float Ak[4], A2[4], iA[4];
+  float Ak[G], A2[G], iA[G];
   {
-    float a4[4] = {-1.f, -1.f, -1.f, -1.f};
-    if (dvalid) load4(p.A + (size_t)d * N + g * 4, a4);
+    float av[G];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      Ak[k] = a4[k];
-      A2[k] = a4[k] * kLog2e;
-      iA[k] = 1.0f / a4[k];
+    for (int k = 0; k < G; ++k) av[k] = -1.f;
+    if (dvalid) loadg<G>(p.A + (size_t)d * N + nbase, av);
+#pragma unroll
+    for (int k = 0; k < G; ++k) {
+      Ak[k] = av[k];
+      A2[k] = av[k] * kLog2e;
+      iA[k] = 1.0f / av[k];
     }
   }
-  const float Dd = (MODE == kModeMain && p.Dskip != nullptr && dvalid) ? p.Dskip[d] : 0.0f;
+  // D skip folded into the partial sum of lane g == 0 of each channel group
+  const float Dd0 = (MODE == kModeMain && p.Dskip != nullptr && dvalid && g == 0) ? p.Dskip[d] : 0.0f;
 
-  float h[4] = {0.f, 0.f, 0.f, 0.f};
-  float P[4] = {1.f, 1.f, 1.f, 1.f};
+  float h[G], P[G];
+#pragma unroll
+  for (int k = 0; k < G; ++k) {
+    h[k] = 0.f;
+    P[k] = 1.f;
+  }
   if (dvalid) {
     const float* src = nullptr;
-    if (p.seg_init != nullptr) src = p.seg_init + (((size_t)b * p.nseg + seg) * p.D + d) * N + g * 4;
-    else if (seg == 0 && p.h_init != nullptr) src = p.h_init + ((size_t)b * p.D + d) * N + g * 4;
-    if (src != nullptr) load4(src, h);
+    if (p.seg_init != nullptr) src = p.seg_init + (((size_t)b * p.nseg + seg) * p.D + d) * N + nbase;
+    else if (seg == 0 && p.h_init != nullptr) src = p.h_init + ((size_t)b * p.D + d) * N + nbase;
+    if (src != nullptr) loadg<G>(src, h);
   }
 
   if (p.use_tma) {
@@ -159,7 +173,7 @@ __global__ void __launch_bounds__(Geo<N>::NT) ssm_fwd_kernel(const __grid_consta
     __syncthreads();
     if (tid == 0) {
       for (int s = 0; s < S::NSTAGE && s < nblk; ++s)
-        fwd_issue_loads<N, T, MODE>(p, smem + s * S::STAGE, &bars[s], d0, t_begin + s * TC, b);
+        fwd_issue_loads<S, MODE>(p, smem + s * S::STAGE, &bars[s], d0, t_begin + s * TC, b);
     }
   }
 
@@ -170,100 +184,95 @@ __global__ void __launch_bounds__(Geo<N>::NT) ssm_fwd_kernel(const __grid_consta
     if (p.use_tma) {
       mbar_wait(&bars[s], (uint32_t)((ib / S::NSTAGE) & 1), p.err);
     } else {
-      fwd_coop_load<N, T, MODE>(p, st, d0, t0, b);
+      fwd_coop_load<S, N, NT, T, MODE>(p, st, d0, t0, b);
       __syncthreads();
     }
-    const T* Xs = reinterpret_cast<const T*>(st + S::OFF_U);
-    const T* DLs = reinterpret_cast<const T*>(st + S::OFF_DT);
-    const T* Zs = reinterpret_cast<const T*>(st + S::OFF_Z);
-    const T* Bs = reinterpret_cast<const T*>(st + S::OFF_B);
-    const T* Cs = reinterpret_cast<const T*>(st + S::OFF_C);
-    T* Ys = reinterpret_cast<T*>(smem + S::OFF_Y + (ib % S::NOUT) * S::ACT);
+    const T* __restrict__ Xs = reinterpret_cast<const T*>(st + S::OFF_U);
+    const T* __restrict__ DLs = reinterpret_cast<const T*>(st + S::OFF_DT);
+    const T* __restrict__ Zs = reinterpret_cast<const T*>(st + S::OFF_Z);
+    const T* __restrict__ Bs = reinterpret_cast<const T*>(st + S::OFF_B);
+    const T* __restrict__ Cs = reinterpret_cast<const T*>(st + S::OFF_C);
+    T* Ys = reinterpret_cast<T*>(smem + S::OFF_Y + (ib % S::NOUT) * 2 * S::OUT);
+    T* YGs = reinterpret_cast<T*>(smem + S::OFF_Y + (ib % S::NOUT) * 2 * S::OUT + S::OUT);
 
-    if (MODE == kModeMain && p.chunk_states != nullptr && dvalid) {
-      // state entering chunk t0 / 16 (t0 is a multiple of 16)
-      *reinterpret_cast<float4*>(p.chunk_states + (((size_t)b * p.nchunks + t0 / TC) * p.D + d) * N + g * 4) =
-          make_float4(h[0], h[1], h[2], h[3]);
-    }
+    if (MODE == kModeMain && p.chunk_states != nullptr && dvalid)   // state entering chunk t0 / 16
+      storeg<G>(p.chunk_states + (((size_t)b * p.nchunks + t0 / TC) * p.D + d) * N + nbase, h);
 
+    // 16 steps.  The lane's partial y (its G states, plus D u on lane 0 of the group) stays
+    // in registers, stored at yp[(t % LPC) YPL + t / LPC] so that after the reduction lane g
+    // holds steps g, g + LPC, ...; the lane also keeps z of those steps.
+    float yp[TC], zk[YPL];
+    // Steps are processed in sub-tiles of SUB: phase A computes everything that does not
+    // depend on the state (decays a, inputs b, C) for SUB steps at once, so the MUFU work of
+    // a sub-tile runs back to back; phase B is only the recurrence and the y accumulation.
 #pragma unroll
-    for (int tg = 0; tg < TC; tg += TG) {
-      float yp[TG];
+    for (int t0s = 0; t0s < TC; t0s += SSM_FWD_SUB) {
+      float av[SSM_FWD_SUB][G], bv[SSM_FWD_SUB][G], cv[SSM_FWD_SUB][G], yd[SSM_FWD_SUB];
 #pragma unroll
-      for (int j = 0; j < TG; ++j) {
-        const int tt = tg + j;
+      for (int q = 0; q < SSM_FWD_SUB; ++q) {
+        const int tt = t0s + q;
         const float uu = to_f32(Xs[tt * DT + dl]);
         const float dtv = to_f32(DLs[tt * DT + dl]);
         const float dtu = dtv * uu;
-        float Bn[4], Cn[4];
-        load4(Bs + tt * N + g * 4, Bn);
-        if (MODE == kModeMain) load4(Cs + tt * N + g * 4, Cn);
-        float acc = 0.0f;
+        float Bn[G];
+        loadg<G>(Bs + tt * N + nbase, Bn);
+        if (MODE == kModeMain) loadg<G>(Cs + tt * N + nbase, cv[q]);
+        yd[q] = Dd0 * uu;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          float a;
-          h[k] = fwd_step<METHOD>(h[k], dtv, uu, dtu, Bn[k], Ak[k], A2[k], iA[k], a);
-          if (MODE == kModeMain) acc = fmaf(Cn[k], h[k], acc);
-          else P[k] *= a;
-        }
-        yp[j] = acc;
-      }
-      if (MODE == kModeMain) {
-        // y over the LPC lanes of the channel: lane g ends with timestep tg + g
-        xpose_reduce<TG, LPC, 1>(yp, lane);
-        const int tt = tg + g;
-        float yv = yp[0];
-        if (p.Dskip != nullptr) yv = fmaf(Dd, to_f32(Xs[tt * DT + dl]), yv);
-        if (p.has_z) {
+        for (int k = 0; k < G; ++k) fwd_coeffs<METHOD>(dtv, uu, dtu, Bn[k], Ak[k], A2[k], iA[k], av[q][k], bv[q][k]);
+        if (MODE == kModeMain && p.has_z) {
           const float zz = to_f32(Zs[tt * DT + dl]);
-          yv *= zz * sigmoid(zz);
+          if (g == tt % LPC) zk[tt / LPC] = zz;
         }
-        Ys[tt * DT + dl] = from_f32<T>(yv);
+      }
+#pragma unroll
+      for (int q = 0; q < SSM_FWD_SUB; ++q) {
+        const int tt = t0s + q;
+        float acc0 = yd[q], acc1 = 0.f;
+#pragma unroll
+        for (int k = 0; k < G; ++k) {
+          h[k] = fwd_apply<METHOD>(h[k], av[q][k], bv[q][k]);
+          if (MODE == kModeMain) {
+            if (k & 1) acc1 = fmaf(cv[q][k], h[k], acc1);
+            else acc0 = fmaf(cv[q][k], h[k], acc0);
+          } else {
+            P[k] *= av[q][k];
+          }
+        }
+        yp[(tt % LPC) * YPL + tt / LPC] = acc0 + acc1;
       }
     }
-
-    if (p.use_tma) {
-      fence_proxy_async_smem();
-      // the store that last read the output buffer written next iteration must be done
-      if (MODE == kModeMain && tid == 0) tma_store_wait_read<1>();
+    if (MODE == kModeMain) {
+      xpose_reduce<TC, LPC, 1>(yp, lane);
+#pragma unroll
+      for (int i = 0; i < YPL; ++i) {
+        const int tt = g + i * LPC;
+        float yv = yp[i];
+        if (p.save_ygate) YGs[tt * OP + dl] = from_f32<T>(yv);
+        if (p.has_z) yv *= zk[i] * sigmoid(zk[i]);
+        Ys[tt * OP + dl] = from_f32<T>(yv);
+      }
     }
     __syncthreads();
-    if (p.use_tma) {
-      if (tid == 0) {
-        if (MODE == kModeMain) {
-          tma_store_3d(&p.tm_y, Ys, d0, t0, b);
-          tma_store_commit();
-        }
-        if (ib + S::NSTAGE < nblk)
-          fwd_issue_loads<N, T, MODE>(p, st, &bars[s], d0, t0 + S::NSTAGE * TC, b);
-      }
-    } else if (MODE == kModeMain) {
-      T* y = static_cast<T*>(const_cast<void*>(p.y.ptr));
-      for (int e = tid; e < TC * DT; e += Gm::NT) {
-        const int tt = e / DT, dd = e % DT;
-        const int t = t0 + tt, dg = d0 + dd;
-        if (t < p.L && dg < p.D) y[b * p.y.sb + (long long)t * p.y.sl + dg] = Ys[e];
-      }
+    if (MODE == kModeMain) {
+      store_tile<NT, OP>(Ys, p.y, b, t0, d0, p.L, p.D);
+      if (p.save_ygate) store_tile<NT, OP>(YGs, p.yg, b, t0, d0, p.L, p.D);
     }
+    if (p.use_tma && tid == 0 && ib + S::NSTAGE < nblk)
+      fwd_issue_loads<S, MODE>(p, st, &bars[s], d0, t0 + S::NSTAGE * TC, b);
   }
 
   if (MODE == kModeMain) {
-    if (dvalid && t_end == p.L && p.last != nullptr)
-      *reinterpret_cast<float4*>(p.last + ((size_t)b * p.D + d) * N + g * 4) = make_float4(h[0], h[1], h[2], h[3]);
+    if (dvalid && t_end == p.L && p.last != nullptr) storeg<G>(p.last + ((size_t)b * p.D + d) * N + nbase, h);
   } else if (dvalid) {
-    const size_t o = (((size_t)b * p.nseg + seg) * p.D + d) * N + g * 4;
-    *reinterpret_cast<float4*>(p.seg_hend + o) = make_float4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<float4*>(p.seg_decay + o) = make_float4(P[0], P[1], P[2], P[3]);
+    const size_t o = (((size_t)b * p.nseg + seg) * p.D + d) * N + nbase;
+    storeg<G>(p.seg_hend + o, h);
+    storeg<G>(p.seg_decay + o, P);
   }
-  if (MODE == kModeMain && p.use_tma && tid == 0) tma_store_wait_all<0>();
 }
 
-// Sequential composition of segment summaries, one thread per (b, d, n):
-//   seg_init[s] = carry;  carry = decay[s] * carry + hend[s]
-__global__ void ssm_carry_kernel(const CarryParams p);
-
-// Host-side launchers (defined per element type in ssm_fwd_<type>.cu).
+// Host-side launcher (defined per element type in ssm_fwd_<type>.cu).  G = states per thread.
 template <typename T>
-cudaError_t launch_fwd(int N, int method, int mode, const FwdParams& p, dim3 grid, cudaStream_t stream);
+cudaError_t launch_fwd(int N, int G, int method, int mode, const FwdParams& p, dim3 grid, cudaStream_t stream);
 
 }  // namespace ssm

@@ -5,44 +5,53 @@
 
 namespace ssm {
 
-template <typename T, int N, int METHOD, int MODE>
+template <typename T, int N, int G, int METHOD, int MODE>
 static cudaError_t launch_fwd_nm(const FwdParams& p, dim3 grid, cudaStream_t stream) {
-  auto kern = ssm_fwd_kernel<N, METHOD, T, MODE>;
-  constexpr int smem = FwdSmem<N, T>::BYTES;
+  auto kern = ssm_fwd_kernel<N, G, METHOD, T, MODE>;
+  constexpr int smem = FwdSmem<N, G, T>::BYTES;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
   }
-  kern<<<grid, Geo<N>::NT, smem, stream>>>(p);
+  kern<<<grid, Geo<N, G>::NT, smem, stream>>>(p);
   return cudaGetLastError();
 }
 
-template <typename T, int N>
+template <typename T, int N, int G>
 static cudaError_t launch_fwd_n(int method, int mode, const FwdParams& p, dim3 grid, cudaStream_t stream) {
   if (mode == kModeMain) {
     switch (method) {
-      case kZOH: return launch_fwd_nm<T, N, kZOH, kModeMain>(p, grid, stream);
-      case kEuler: return launch_fwd_nm<T, N, kEuler, kModeMain>(p, grid, stream);
-      case kBilinear: return launch_fwd_nm<T, N, kBilinear, kModeMain>(p, grid, stream);
+      case kZOH: return launch_fwd_nm<T, N, G, kZOH, kModeMain>(p, grid, stream);
+      case kEuler: return launch_fwd_nm<T, N, G, kEuler, kModeMain>(p, grid, stream);
+      case kBilinear: return launch_fwd_nm<T, N, G, kBilinear, kModeMain>(p, grid, stream);
     }
   } else {
     switch (method) {
-      case kZOH: return launch_fwd_nm<T, N, kZOH, kModeSummary>(p, grid, stream);
-      case kEuler: return launch_fwd_nm<T, N, kEuler, kModeSummary>(p, grid, stream);
-      case kBilinear: return launch_fwd_nm<T, N, kBilinear, kModeSummary>(p, grid, stream);
+      case kZOH: return launch_fwd_nm<T, N, G, kZOH, kModeSummary>(p, grid, stream);
+      case kEuler: return launch_fwd_nm<T, N, G, kEuler, kModeSummary>(p, grid, stream);
+      case kBilinear: return launch_fwd_nm<T, N, G, kBilinear, kModeSummary>(p, grid, stream);
     }
   }
   return cudaErrorInvalidValue;
 }
 
+// G = 2 (twice the threads for small grids) is built for N = 8 and 16.
 template <>
-cudaError_t launch_fwd<SSM_ELEM>(int N, int method, int mode, const FwdParams& p, dim3 grid, cudaStream_t stream) {
+cudaError_t launch_fwd<SSM_ELEM>(int N, int G, int method, int mode, const FwdParams& p, dim3 grid,
+                                 cudaStream_t stream) {
+  if (G == 2) {
+    switch (N) {
+      case 8: return launch_fwd_n<SSM_ELEM, 8, 2>(method, mode, p, grid, stream);
+      case 16: return launch_fwd_n<SSM_ELEM, 16, 2>(method, mode, p, grid, stream);
+    }
+    return cudaErrorInvalidValue;
+  }
   switch (N) {
-    case 4: return launch_fwd_n<SSM_ELEM, 4>(method, mode, p, grid, stream);
-    case 8: return launch_fwd_n<SSM_ELEM, 8>(method, mode, p, grid, stream);
-    case 16: return launch_fwd_n<SSM_ELEM, 16>(method, mode, p, grid, stream);
-    case 32: return launch_fwd_n<SSM_ELEM, 32>(method, mode, p, grid, stream);
-    case 64: return launch_fwd_n<SSM_ELEM, 64>(method, mode, p, grid, stream);
+    case 4: return launch_fwd_n<SSM_ELEM, 4, 4>(method, mode, p, grid, stream);
+    case 8: return launch_fwd_n<SSM_ELEM, 8, 4>(method, mode, p, grid, stream);
+    case 16: return launch_fwd_n<SSM_ELEM, 16, 4>(method, mode, p, grid, stream);
+    case 32: return launch_fwd_n<SSM_ELEM, 32, 4>(method, mode, p, grid, stream);
+    case 64: return launch_fwd_n<SSM_ELEM, 64, 4>(method, mode, p, grid, stream);
   }
   return cudaErrorInvalidValue;
 }

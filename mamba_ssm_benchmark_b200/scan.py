@@ -70,7 +70,8 @@ class SelectiveScanFn(torch.autograd.Function):
 
     Saves the inputs plus the state entering every 16-step chunk (B, ceil(L/16), D, N) fp32,
     from which the backward kernel recomputes states in registers (the reference recomputes
-    all (B, L, D_tile, N) states into HBM instead, kernels/triton_scan.py:305-309).
+    all (B, L, D_tile, N) states into HBM instead, kernels/triton_scan.py:305-309), and, when z
+    is given, the gate's input y + x*D, which the backward needs for dz.
     """
 
     @staticmethod
@@ -83,22 +84,24 @@ class SelectiveScanFn(torch.autograd.Function):
         need_bwd = any(ctx.needs_input_grad[:8])
         nchunks = -(-L // CHUNK)
         cs = torch.empty((Bsz, nchunks, Dch, N), dtype=torch.float32, device=dev) if need_bwd else None
+        # the gate's input (y + x D), needed by the backward to form dz
+        yg = torch.empty((Bsz, L, Dch), dtype=x.dtype, device=dev) if (need_bwd and z is not None) else None
         wsb = nat.fwd_workspace_bytes(Bsz, L, Dch, N)
         ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
         with torch.cuda.device(dev):
             rc = nat.lib().ssm_scan_fwd(
                 Bsz, L, Dch, N, nat.METHODS[method], nat.view3(x), nat.view3(delta), nat.ptr(A),
                 nat.view3(Bm), nat.view3(Cm), nat.ptr(D), nat.view3(z), nat.ptr(h0),
-                nat.view3(y), nat.ptr(last), nat.ptr(cs), ws.data_ptr(), wsb, nat.stream_of(dev))
+                nat.view3(y), nat.view3(yg), nat.ptr(last), nat.ptr(cs), ws.data_ptr(), wsb, nat.stream_of(dev))
         nat.check(rc, "ssm_scan_fwd")
         if need_bwd:
-            ctx.save_for_backward(x, delta, A, Bm, Cm, h0, D, z, cs)
+            ctx.save_for_backward(x, delta, A, Bm, Cm, h0, D, z, cs, yg)
         ctx.method = method
         return y, last
 
     @staticmethod
     def backward(ctx, dy, dlast):
-        x, delta, A, Bm, Cm, h0, D, z, cs = ctx.saved_tensors
+        x, delta, A, Bm, Cm, h0, D, z, cs, yg = ctx.saved_tensors
         Bsz, L, Dch = x.shape
         N = A.shape[1]
         dev = x.device
@@ -118,7 +121,7 @@ class SelectiveScanFn(torch.autograd.Function):
             rc = nat.lib().ssm_scan_bwd(
                 Bsz, L, Dch, N, nat.METHODS[ctx.method], nat.view3(x), nat.view3(delta), nat.ptr(A),
                 nat.view3(Bm), nat.view3(Cm), nat.ptr(D), nat.view3(z), nat.ptr(h0), nat.ptr(cs),
-                nat.view3(dy), nat.ptr(dlast), nat.view3(du), nat.view3(ddelta), nat.ptr(dA),
+                nat.view3(yg), nat.view3(dy), nat.ptr(dlast), nat.view3(du), nat.view3(ddelta), nat.ptr(dA),
                 nat.view3(dB), nat.view3(dC), nat.ptr(dD), nat.view3(dz), nat.ptr(dh0),
                 ws.data_ptr(), wsb, nat.stream_of(dev))
         nat.check(rc, "ssm_scan_bwd")

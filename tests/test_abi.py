@@ -53,10 +53,10 @@ def test_bad_arguments_raise_value_error():
         nat.bwd_workspace_bytes(1, 0, 32, 16)
     lib = nat.lib()
     v = nat.NULL_VIEW
-    rc = lib.ssm_scan_fwd(1, 16, 32, 16, 7, v, v, None, v, v, None, v, None, v, None, None, None, 0, None)
+    rc = lib.ssm_scan_fwd(1, 16, 32, 16, 7, v, v, None, v, v, None, v, None, v, v, None, None, None, 0, None)
     assert rc == nat.SSM_ERR_INVALID
     assert b"method" in lib.ssm_last_error_message()
-    rc = lib.ssm_scan_fwd(1, 16, 32, 16, 0, v, v, None, v, v, None, v, None, v, None, None, None, 0, None)
+    rc = lib.ssm_scan_fwd(1, 16, 32, 16, 0, v, v, None, v, v, None, v, None, v, v, None, None, None, 0, None)
     assert rc == nat.SSM_ERR_INVALID and b"u is required" in lib.ssm_last_error_message()
 
 
@@ -65,7 +65,7 @@ def test_mixed_dtypes_are_rejected_by_the_abi():
     u = nat.SsmView(ctypes.c_void_p(256), nat.SSM_F32, 0, 16 * 32, 32)
     d = nat.SsmView(ctypes.c_void_p(256), nat.SSM_BF16, 0, 16 * 32, 32)
     rc = lib.ssm_scan_fwd(1, 16, 32, 16, 0, u, d, ctypes.c_void_p(256), u, u, None, nat.NULL_VIEW, None, u,
-                          None, None, None, 0, None)
+                          nat.NULL_VIEW, None, None, None, 0, None)
     assert rc == nat.SSM_ERR_DTYPE
 
 

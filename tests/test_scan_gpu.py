@@ -216,3 +216,17 @@ def test_dB_dC_linearity_over_channel_groups():
         acc_C += r["dCm"]
     assert O.normwise_error(acc_B, full["dBm"]) < 1e-5
     assert O.normwise_error(acc_C, full["dCm"]) < 1e-5
+
+
+@pytest.mark.parametrize("states_per_thread", ["2", "4"])
+@pytest.mark.parametrize("shape", [(2, 37, 50, 16), (3, 130, 96, 8), (16, 64, 128, 16), (1, 200, 64, 16)],
+                         ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("method", METHODS)
+def test_both_thread_geometries(states_per_thread, shape, method, monkeypatch):
+    """The kernels exist for G = 2 and G = 4 states per thread (the host picks by grid size);
+    both must match the oracle, including the fused gate and an initial state."""
+    monkeypatch.setenv("SSM_B200_STATES_PER_THREAD", states_per_thread)
+    ins = make_inputs(*shape, seed=7, dist="test", h0=True, dlast=True)
+    got = H.run(H.ours, ins, method, DEV, torch.float32, True, True, w2=ins["dlast"])
+    ref = H.run(H.oracle, ins, method, "cpu", torch.float32, True, True, w2=ins["dlast"])
+    H.compare(got, ref)
