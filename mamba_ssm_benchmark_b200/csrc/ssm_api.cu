@@ -16,7 +16,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "../../include/ssm_b200.h"
+#include "ssm_b200.h"
 #include "ssm_bwd.cuh"
 #include "ssm_fwd.cuh"
 
@@ -130,18 +130,19 @@ int sm_count() {
   return n;
 }
 
-// States per thread.  G = 4 keeps more independent recurrences per thread; G = 2 doubles the
-// thread count, which pays off when the (batch x channel) grid at G = 4 would give the GPU
-// fewer than 16 warps per SM (the recurrences are latency-bound at low occupancy).  Built for
-// N = 8 and 16.  SSM_B200_STATES_PER_THREAD=2|4 overrides the choice (tuning, tests).
+// States per thread.  G = 4 is the default: with fewer states per thread the shared-memory
+// traffic per element (B, C and the per-channel inputs are re-read by every lane) and the
+// reduction work grow faster than the extra warps help, which measurements on B200 confirmed
+// for every shape tried.  G = 2 is built for N = 8 and 16; SSM_B200_STATES_PER_THREAD=2|4
+// overrides the choice (tuning, tests).
 int choose_g(int64_t B, int64_t D, int64_t N) {
+  (void)B;
+  (void)D;
   if (N != 8 && N != 16) return 4;
   if (const char* env = getenv("SSM_B200_STATES_PER_THREAD")) {
     if (env[0] == '2') return 2;
-    if (env[0] == '4') return 4;
   }
-  const int64_t threads4 = B * ((D + 31) / 32) * 32 * N / 4;
-  return threads4 < (int64_t)sm_count() * 512 ? 2 : 4;
+  return 4;
 }
 
 // Sequence split of the forward: S segments of seg_len steps (a multiple of 16).  Splitting
@@ -263,14 +264,18 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   p.nchunks = (int)((L + kChunk - 1) / kChunk);
   p.has_z = z.ptr != nullptr;
 
+  // one warp per CTA: its TMA boxes are CPW channels wide, widened to 16 bytes of channels
+  const int G = choose_g(B, D, N);
+  const int cpw = (int)(32 * G / N);
+  const int bxc = std::max<int>(cpw, (int)(16 / esize(dt)));
   bool use_tma = tma_ok(u, B, L, D) && tma_ok(delta, B, L, D) && tma_ok(Bm, B, L, N);
   if (phase != 1) use_tma = use_tma && tma_ok(Cm, B, L, N) && (!p.has_z || tma_ok(z, B, L, D));
   if (use_tma) {
-    bool ok = make_map(&p.tm_u, u, B, L, D, 32, kChunk) && make_map(&p.tm_dt, delta, B, L, D, 32, kChunk) &&
+    bool ok = make_map(&p.tm_u, u, B, L, D, bxc, kChunk) && make_map(&p.tm_dt, delta, B, L, D, bxc, kChunk) &&
               make_map(&p.tm_B, Bm, B, L, N, (int)N, kChunk);
     if (phase != 1) {
       ok = ok && make_map(&p.tm_C, Cm, B, L, N, (int)N, kChunk);
-      if (p.has_z) ok = ok && make_map(&p.tm_z, z, B, L, D, 32, kChunk);
+      if (p.has_z) ok = ok && make_map(&p.tm_z, z, B, L, D, bxc, kChunk);
     }
     use_tma = ok;
   }
@@ -283,7 +288,6 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   const unsigned ndt = (unsigned)((D + 31) / 32);
   const dim3 grid(ndt, (unsigned)S, (unsigned)B);
   const bool bf = dt == SSM_BF16;
-  const int G = choose_g(B, D, N);
   auto launch = [&](int mode, const FwdParams& q) {
     return bf ? launch_fwd<__nv_bfloat16>((int)N, G, method, mode, q, grid, stream)
               : launch_fwd<float>((int)N, G, method, mode, q, grid, stream);

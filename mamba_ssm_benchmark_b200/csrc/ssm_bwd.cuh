@@ -128,11 +128,11 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
   using S = BwdSmem<N, G, T>;
   constexpr int TC = Gm::TC, DT = Gm::DT, LPC = Gm::LPC, CPW = Gm::CPW, NW = Gm::NW, NT = Gm::NT;
   constexpr int OP = S::OP, OPF = S::OPF;
+  constexpr int NP = G / 2;                            // state pairs per thread
   constexpr int LC = ilog2(CPW), LG = ilog2(G);
   constexpr int NSLOT = LC < LG ? LC : LG;             // slot-splitting stages (select-free)
-  constexpr int KF = G >> NSLOT;                       // live slots after them
   constexpr bool QSTAGE = LC > LG;                     // a dB / dC splitting stage follows
-  constexpr int BCPL = QSTAGE ? 1 : 2 * KF;            // dB|dC values per lane at the end
+  constexpr int BCPL = QSTAGE ? 1 : (LC == LG ? 2 : 4);   // dB|dC values per lane at the end
   constexpr int BCDUP = (LC > LG + 1) ? (1 << (LC - LG - 1)) : 1;
   // (du, ddelta) over the LPC lanes of a channel, 4 steps per transposition: V = 8 values
   constexpr int QV = 8;
@@ -160,23 +160,36 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
 #pragma unroll
   for (int s2 = 0; s2 < NSLOT; ++s2) perm |= ((c >> (LC - 1 - s2)) & 1) << (LG - 1 - s2);
 
-  float Ak[G], A2[G], iA[G];
+  auto slot_load = [&](const float* src, float2 (&o)[NP]) {   // G values at src, slot order
 #pragma unroll
-  for (int j = 0; j < G; ++j) {
-    const float a = dvalid ? p.A[(size_t)d * N + nbase + (j ^ perm)] : -1.f;
-    Ak[j] = a;
-    A2[j] = a * kLog2e;
-    iA[j] = 1.0f / a;
+    for (int i = 0; i < NP; ++i)
+      o[i] = dvalid ? make_float2(src[(2 * i) ^ perm], src[(2 * i + 1) ^ perm]) : bc2(0.f);
+  };
+  float2 Ak[NP], A2[NP], iA[NP], niA[NP];
+  {
+    float2 av[NP];
+    slot_load(p.A + (size_t)d * N + nbase, av);
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      if (!dvalid) av[i] = bc2(-1.f);
+      Ak[i] = av[i];
+      A2[i] = mul2(av[i], bc2(kLog2e));
+      iA[i] = make_float2(1.0f / av[i].x, 1.0f / av[i].y);
+      niA[i] = make_float2(-iA[i].x, -iA[i].y);
+    }
   }
   const float Dd = (p.Dskip != nullptr && dvalid) ? p.Dskip[d] : 0.0f;
   const size_t bd = ((size_t)b * p.D + d) * N + nbase;
 
-  float dh[G], dAA[G];
+  float2 dh[NP], dAA[NP];
+  if (p.dlast != nullptr) {
+    slot_load(p.dlast + bd, dh);
+  } else {
 #pragma unroll
-  for (int j = 0; j < G; ++j) {
-    dh[j] = (dvalid && p.dlast != nullptr) ? p.dlast[bd + (j ^ perm)] : 0.f;
-    dAA[j] = 0.f;
+    for (int i = 0; i < NP; ++i) dh[i] = bc2(0.f);
   }
+#pragma unroll
+  for (int i = 0; i < NP; ++i) dAA[i] = bc2(0.f);
   float dDacc = 0.0f;
 
   if (p.use_tma) {
@@ -192,25 +205,21 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
     }
   }
 
-  auto load_state = [&](int ch, float (&o)[G]) {
-    const float* src = p.chunk_states + (((size_t)b * nch + ch) * p.D + d) * N + nbase;
-#pragma unroll
-    for (int j = 0; j < G; ++j) o[j] = dvalid ? src[j ^ perm] : 0.f;
-  };
-  float hs[G];
-  load_state(nch - 1, hs);
+  auto cs_ptr = [&](int ch) { return p.chunk_states + (((size_t)b * nch + ch) * p.D + d) * N + nbase; };
+  float2 hs[NP];
+  slot_load(cs_ptr(nch - 1), hs);
 
   for (int i = 0; i < nch; ++i) {
     const int ch = nch - 1 - i;
     const int s = i % S::NSTAGE;
     const int t0 = ch * TC;
     unsigned char* st = smem + s * S::STAGE;
-    float hs_next[G];
+    float2 hs_next[NP];
     if (ch > 0) {
-      load_state(ch - 1, hs_next);
+      slot_load(cs_ptr(ch - 1), hs_next);
     } else {
 #pragma unroll
-      for (int j = 0; j < G; ++j) hs_next[j] = 0.f;
+      for (int k = 0; k < NP; ++k) hs_next[k] = bc2(0.f);
     }
 
     if (p.use_tma) {
@@ -246,11 +255,18 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
       }
       const T* Bs = reinterpret_cast<const T*>(st + S::OFF_B);
       const T* Cs = reinterpret_cast<const T*>(st + S::OFF_C);
-      for (int e = tid; e < G * TC * N; e += NT) {
-        const int pm = e / (TC * N), r = e % (TC * N);
-        const int n = r % N, src = (r - n) + ((n & ~(G - 1)) | ((n & (G - 1)) ^ pm));
-        SBP[e] = to_f32(Bs[src]);
-        SCP[e] = to_f32(Cs[src]);
+      for (int e = tid; e < 2 * TC * N / G; e += NT) {    // one G-group of B or C per iteration
+        const int which = e / (TC * N / G), r = (e % (TC * N / G)) * G;
+        float v[G];
+        loadg<G>((which ? Cs : Bs) + r, v);
+        float* dst = (which ? SCP : SBP) + r;
+#pragma unroll
+        for (int pm = 0; pm < G; ++pm) {
+          float w[G];
+#pragma unroll
+          for (int j = 0; j < G; ++j) w[j] = v[j ^ pm];
+          storeg<G>(dst + pm * TC * N, w);
+        }
       }
     }
     __syncthreads();
@@ -259,47 +275,46 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
     float* __restrict__ Acache = SAC + tid * G;
 
     // (3) recompute the chunk's states from its checkpoint; cache the decays (or the states)
-    float H[S::HSMEM ? 1 : TC][G];
+    float2 H[S::HSMEM ? 1 : TC][NP];
     {
-      float hc[G];
+      float2 hc[NP];
 #pragma unroll
-      for (int k = 0; k < G; ++k) hc[k] = hs[k];
+      for (int k = 0; k < NP; ++k) hc[k] = hs[k];
 #pragma unroll
       for (int j = 0; j < TC; ++j) {
         const float uu = to_f32(Xs[j * DT + dl]);
         const float dtv = to_f32(DLs[j * DT + dl]);
-        const float dtu = dtv * uu;
-        float Bn[G], av[G];
-        loadg<G>(Bp + j * N, Bn);
+        const float2 u2 = bc2(uu), dt2 = bc2(dtv), dtu2 = bc2(dtv * uu);
+        float2 Bn[NP], av[NP];
+        loadp<G>(Bp + j * N, Bn);
 #pragma unroll
-        for (int k = 0; k < G; ++k) {
+        for (int k = 0; k < NP; ++k) {
           if (METHOD == kZOH) {
-            const float a = ex2(dtv * A2[k]);
-            const float gg = (Bn[k] * uu) * iA[k];
-            hc[k] = fmaf(a, hc[k] + gg, -gg);
+            const float2 a = ex2x2(mul2(dt2, A2[k]));
+            const float2 ng = mul2(mul2(Bn[k], u2), niA[k]);
+            hc[k] = fma2(a, fma2(ng, bc2(-1.0f), hc[k]), ng);
             av[k] = a;
           } else if (METHOD == kEuler) {
-            const float a = ex2(dtv * A2[k]);
-            hc[k] = fmaf(a, hc[k], dtu * Bn[k]);
+            const float2 a = ex2x2(mul2(dt2, A2[k]));
+            hc[k] = fma2(a, hc[k], mul2(dtu2, Bn[k]));
             av[k] = a;
           } else {
-            const float zz = dtv * Ak[k];
-            const float w = rcp(fmaf(-0.5f, zz, 1.0f));
-            hc[k] = fmaf(fmaf(0.5f, zz, 1.0f) * w, hc[k], (dtu * Bn[k]) * w);
+            const float2 zz = mul2(dt2, Ak[k]);
+            const float2 w = rcpx2(fma2(bc2(-0.5f), zz, bc2(1.0f)));
+            hc[k] = fma2(mul2(fma2(bc2(0.5f), zz, bc2(1.0f)), w), hc[k], mul2(mul2(dtu2, Bn[k]), w));
             av[k] = w;   // bilinear caches w = 1/(1 - z/2); a = (1 + z/2) w
           }
           if (!S::HSMEM) H[S::HSMEM ? 0 : j][k] = hc[k];
         }
-        if (S::ACACHE) storeg<G>(Acache + j * NT * G, av);
-        if (S::HSMEM) storeg<G>(Acache + j * NT * G, hc);
+        if (S::ACACHE) storep<G>(Acache + j * NT * G, av);
+        if (S::HSMEM) storep<G>(Acache + j * NT * G, hc);
       }
     }
 
-    // (4) reverse adjoint through the chunk
-    float keep_q[TC / 4][QPL];   // (du, ddelta) results, 4 steps per group
-    float keep_bc[TC][BCPL];     // dB | dC results, per step
-    float hnext[G];              // HSMEM: state of step j, carried from step j + 1's load
-    if (S::HSMEM) loadg<G>(Acache + (TC - 1) * NT * G, hnext);
+    // (4) reverse adjoint through the chunk.  du and dB are accumulated negated (-du, -dB),
+    // which turns every per-state update into one packed FMA.
+    float2 hnext[NP];            // HSMEM: state of step j, carried from step j + 1's load
+    if (S::HSMEM) loadp<G>(Acache + (TC - 1) * NT * G, hnext);
 #pragma unroll
     for (int jg = TC / 4 - 1; jg >= 0; --jg) {
       float red[QV];
@@ -309,135 +324,136 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
         const float uu = to_f32(Xs[j * DT + dl]);
         const float dtv = to_f32(DLs[j * DT + dl]);
         const float dys = SDYS[j * OPF + dl];
-        float Bn[G], Cn[G], av[G];
-        loadg<G>(Bp + j * N, Bn);
-        loadg<G>(Cp + j * N, Cn);
+        const float2 u2 = bc2(uu), dt2 = bc2(dtv), dys2 = bc2(dys);
+        float2 Bn[NP], Cn[NP], av[NP], hprev[NP];
+        loadp<G>(Bp + j * N, Bn);
+        loadp<G>(Cp + j * N, Cn);
         if (S::ACACHE) {
-          loadg<G>(Acache + j * NT * G, av);
+          loadp<G>(Acache + j * NT * G, av);
         } else {
 #pragma unroll
-          for (int k = 0; k < G; ++k)
-            av[k] = (METHOD == kBilinear) ? rcp(fmaf(-0.5f * dtv, Ak[k], 1.0f)) : ex2(dtv * A2[k]);
+          for (int k = 0; k < NP; ++k)
+            av[k] = (METHOD == kBilinear) ? rcpx2(fma2(mul2(bc2(-0.5f), dt2), Ak[k], bc2(1.0f)))
+                                          : ex2x2(mul2(dt2, A2[k]));
         }
-        float duv = 0.f, ddtv = 0.f;
-        float bB[G], bC[G];
-        float hprev[G];
         if (S::HSMEM) {
           if (j > 0) {
-            loadg<G>(Acache + (j > 0 ? j - 1 : 0) * NT * G, hprev);
+            loadp<G>(Acache + (j > 0 ? j - 1 : 0) * NT * G, hprev);
           } else {
 #pragma unroll
-            for (int k = 0; k < G; ++k) hprev[k] = hs[k];
+            for (int k = 0; k < NP; ++k) hprev[k] = hs[k];
           }
         }
+        float2 duN = bc2(0.f), ddt = bc2(0.f);
+        float2 bBN[NP], bC[NP];
 #pragma unroll
-        for (int k = 0; k < G; ++k) {
-          const float ht = S::HSMEM ? hnext[k] : H[S::HSMEM ? 0 : j][k];
-          const float hp = S::HSMEM ? hprev[k] : ((j > 0) ? H[(S::HSMEM || j == 0) ? 0 : j - 1][k] : hs[k]);
-          const float Bu = Bn[k] * uu;
-          dh[k] = fmaf(dys, Cn[k], dh[k]);
-          bC[k] = dys * ht;
+        for (int k = 0; k < NP; ++k) {
+          const float2 ht = S::HSMEM ? hnext[k] : H[S::HSMEM ? 0 : j][k];
+          const float2 hp = S::HSMEM ? hprev[k] : ((j > 0) ? H[(S::HSMEM || j == 0) ? 0 : j - 1][k] : hs[k]);
+          const float2 Bu = mul2(Bn[k], u2);
+          dh[k] = fma2(dys2, Cn[k], dh[k]);
+          bC[k] = mul2(dys2, ht);
           if (METHOD == kZOH) {
-            const float q = dh[k] * av[k];
-            const float sv = q * fmaf(Ak[k], hp, Bu);
-            ddtv += sv;
-            const float pp = (q - dh[k]) * iA[k];
-            duv = fmaf(pp, Bn[k], duv);
-            bB[k] = pp * uu;
-            dAA[k] = fmaf(dtv, sv, dAA[k]);
-            dAA[k] = fmaf(-pp, Bu, dAA[k]);
+            const float2 q = mul2(dh[k], av[k]);
+            const float2 sv = mul2(q, fma2(Ak[k], hp, Bu));
+            ddt = add2(ddt, sv);
+            const float2 npp = mul2(fma2(q, bc2(-1.0f), dh[k]), iA[k]);   // -(dh coef)
+            duN = fma2(npp, Bn[k], duN);
+            bBN[k] = mul2(npp, u2);
+            dAA[k] = fma2(dt2, sv, dAA[k]);
+            dAA[k] = fma2(npp, Bu, dAA[k]);
             dh[k] = q;
           } else if (METHOD == kEuler) {
-            const float q = dh[k] * av[k];
-            const float sv = fmaf(q * Ak[k], hp, dh[k] * Bu);
-            ddtv += sv;
-            const float pp = dh[k] * dtv;
-            duv = fmaf(pp, Bn[k], duv);
-            bB[k] = pp * uu;
-            dAA[k] = fmaf(dtv * q, hp, dAA[k]);
+            const float2 q = mul2(dh[k], av[k]);
+            const float2 sv = fma2(mul2(q, Ak[k]), hp, mul2(dh[k], Bu));
+            ddt = add2(ddt, sv);
+            const float2 npp = mul2(dh[k], bc2(-dtv));
+            duN = fma2(npp, Bn[k], duN);
+            bBN[k] = mul2(npp, u2);
+            dAA[k] = fma2(mul2(dt2, q), hp, dAA[k]);
             dh[k] = q;
           } else {
-            const float w = av[k];
-            const float zz = dtv * Ak[k];
-            const float a = fmaf(0.5f, zz, 1.0f) * w;
-            const float dhw2 = dh[k] * w * w;
-            const float sv = dhw2 * fmaf(Ak[k], hp, Bu);
-            ddtv += sv;
-            const float pp = dh[k] * dtv * w;
-            duv = fmaf(pp, Bn[k], duv);
-            bB[k] = pp * uu;
-            dAA[k] = fmaf(dtv * dhw2, fmaf(0.5f * dtv, Bu, hp), dAA[k]);
-            dh[k] = dh[k] * a;
+            const float2 w = av[k];
+            const float2 zz = mul2(dt2, Ak[k]);
+            const float2 a = mul2(fma2(bc2(0.5f), zz, bc2(1.0f)), w);
+            const float2 dhw2 = mul2(mul2(dh[k], w), w);
+            const float2 sv = mul2(dhw2, fma2(Ak[k], hp, Bu));
+            ddt = add2(ddt, sv);
+            const float2 npp = mul2(mul2(dh[k], bc2(-dtv)), w);
+            duN = fma2(npp, Bn[k], duN);
+            bBN[k] = mul2(npp, u2);
+            dAA[k] = fma2(mul2(dt2, dhw2), fma2(bc2(0.5f * dtv), Bu, hp), dAA[k]);
+            dh[k] = mul2(dh[k], a);
           }
         }
-        // dB | dC over the warp's channels: slot-splitting stages first (a fixed register
-        // slot is sent on every lane thanks to the state permutation), then one stage that
-        // splits dB from dC, then all-reduce stages for the remaining channel bits.
+        // dB | dC over the warp's channels: slot-splitting stages first (a fixed register slot
+        // is sent on every lane thanks to the state permutation), then one stage that splits
+        // dB from dC, then all-reduce stages for the remaining channel bits.
+        if constexpr (G == 4 && LC >= 1) {   // slot bit 1: keep pair 0, receive the partner's pair 1
+          constexpr int m = (CPW / 2) * LPC;
+          bBN[0] = add2(bBN[0], make_float2(__shfl_xor_sync(0xffffffffu, bBN[NP - 1].x, m),
+                                            __shfl_xor_sync(0xffffffffu, bBN[NP - 1].y, m)));
+          bC[0] = add2(bC[0], make_float2(__shfl_xor_sync(0xffffffffu, bC[NP - 1].x, m),
+                                          __shfl_xor_sync(0xffffffffu, bC[NP - 1].y, m)));
+        }
+        float keep[BCPL];
+        if constexpr (LC >= LG) {            // slot bit 0: (-dB, dC) of slot 0
+          constexpr int m = (CPW >> LG) * LPC;
+          const float2 t2 = add2(make_float2(bBN[0].x, bC[0].x),
+                                 make_float2(__shfl_xor_sync(0xffffffffu, bBN[0].y, m),
+                                             __shfl_xor_sync(0xffffffffu, bC[0].y, m)));
+          if constexpr (QSTAGE) {
+            constexpr int m3 = (CPW >> (LG + 1)) * LPC;
+            const bool up = (c >> (LC - LG - 1)) & 1;
+            const float send = up ? t2.x : t2.y;
+            float kv = (up ? t2.y : t2.x) + __shfl_xor_sync(0xffffffffu, send, m3);
 #pragma unroll
-        for (int s2 = 0; s2 < NSLOT; ++s2) {
-          const int m = (CPW >> (s2 + 1)) * LPC;
-          const int half = G >> (s2 + 1);
-#pragma unroll
-          for (int k = 0; k < half; ++k) {
-            bB[k] += __shfl_xor_sync(0xffffffffu, bB[k + half], m);
-            bC[k] += __shfl_xor_sync(0xffffffffu, bC[k + half], m);
+            for (int mm = CPW >> (LG + 2); mm >= 1; mm >>= 1) kv += __shfl_xor_sync(0xffffffffu, kv, mm * LPC);
+            keep[0] = kv;
+          } else {
+            keep[0] = t2.x;
+            keep[(1) % BCPL] = t2.y;
+          }
+        } else {                             // CPW = 2, G = 4: slots 0 and 1 remain
+          keep[0] = bBN[0].x;
+          keep[1 % BCPL] = bBN[0].y;
+          keep[2 % BCPL] = bC[0].x;
+          keep[3 % BCPL] = bC[0].y;
+        }
+        {
+          float* dst = SRED + (j * NW + warp) * 2 * N;
+          if constexpr (QSTAGE) {
+            if ((c & (BCDUP - 1)) == 0) {
+              const int q = (c >> (LC - LG - 1)) & 1;
+              dst[q * N + nbase + perm] = q ? keep[0] : -keep[0];
+            }
+          } else if constexpr (LC == LG) {
+            dst[nbase + perm] = -keep[0];
+            dst[N + nbase + perm] = keep[1 % BCPL];
+          } else {
+            dst[nbase + (0 ^ perm)] = -keep[0];
+            dst[nbase + (1 ^ perm)] = -keep[1 % BCPL];
+            dst[N + nbase + (0 ^ perm)] = keep[2 % BCPL];
+            dst[N + nbase + (1 ^ perm)] = keep[3 % BCPL];
           }
         }
-        if constexpr (QSTAGE) {
-          constexpr int m = (CPW >> (LG + 1)) * LPC;
-          const bool up = (c >> (LC - LG - 1)) & 1;
-          const float send = up ? bB[0] : bC[0];
-          float kv = (up ? bC[0] : bB[0]) + __shfl_xor_sync(0xffffffffu, send, m);
-#pragma unroll
-          for (int mm = CPW >> (LG + 2); mm >= 1; mm >>= 1) kv += __shfl_xor_sync(0xffffffffu, kv, mm * LPC);
-          keep_bc[j][0] = kv;
-        } else {
-#pragma unroll
-          for (int k = 0; k < KF; ++k) {
-            keep_bc[j][k] = bB[k];
-            keep_bc[j][(KF + k) % BCPL] = bC[k];
-          }
-        }
-        red[jj * 2 + 0] = duv;
-        red[jj * 2 + 1] = ddtv;
+        red[jj * 2 + 0] = -(duN.x + duN.y);
+        red[jj * 2 + 1] = ddt.x + ddt.y;
         if (S::HSMEM) {
 #pragma unroll
-          for (int k = 0; k < G; ++k) hnext[k] = hprev[k];
+          for (int k = 0; k < NP; ++k) hnext[k] = hprev[k];
         }
       }
       xpose_reduce<QV, LPC, 1>(red, lane);
-#pragma unroll
-      for (int v = 0; v < QPL; ++v) keep_q[jg][v] = red[v];
-    }
-
-    // chunk epilogue: dB|dC per (step, warp) into shared memory, du / ddelta tiles
-#pragma unroll
-    for (int j = 0; j < TC; ++j) {
-      float* dst = SRED + (j * NW + warp) * 2 * N;
-      if constexpr (QSTAGE) {
-        if ((c & (BCDUP - 1)) == 0) {
-          const int q = (c >> (LC - LG - 1)) & 1;
-          dst[q * N + nbase + perm] = keep_bc[j][0];
-        }
-      } else {
-#pragma unroll
-        for (int k = 0; k < KF; ++k) {
-          dst[nbase + (k ^ perm)] = keep_bc[j][k];
-          dst[N + nbase + (k ^ perm)] = keep_bc[j][(KF + k) % BCPL];
-        }
-      }
-    }
-    if ((g % QDUP) == 0) {
-#pragma unroll
-      for (int jg = 0; jg < TC / 4; ++jg) {
+      if ((g % QDUP) == 0) {
 #pragma unroll
         for (int v = 0; v < QPL; ++v) {
           const int idx = (g / QDUP) * QPL + v;   // value index: step jg*4 + idx/2, quantity idx%2
           const int j = jg * 4 + (idx >> 1);
           if (idx & 1) {
-            DDTo[j * OP + dl] = from_f32<T>(keep_q[jg][v]);
+            DDTo[j * OP + dl] = from_f32<T>(red[v]);
           } else {
-            DUo[j * OP + dl] = from_f32<T>(fmaf(Dd, SDYS[j * OPF + dl], keep_q[jg][v]));
+            DUo[j * OP + dl] = from_f32<T>(fmaf(Dd, SDYS[j * OPF + dl], red[v]));
           }
         }
       }
@@ -461,7 +477,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
     store_tile<NT, OP>(DDTo, p.ddt, b, t0, d0, p.L, p.D);
     if (p.has_z) store_tile<NT, OP>(DZo, p.dz, b, t0, d0, p.L, p.D);
 #pragma unroll
-    for (int k = 0; k < G; ++k) hs[k] = hs_next[k];
+    for (int k = 0; k < NP; ++k) hs[k] = hs_next[k];
   }
 
   // per-(b, d) partials; ssm_bwd_finalize sums them over b in fixed order
@@ -469,10 +485,14 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
   __syncthreads();
   if (dvalid) {
 #pragma unroll
-    for (int j = 0; j < G; ++j) {
-      const size_t o = bd + (j ^ perm);
-      p.part_A[o] = (METHOD == kZOH) ? dAA[j] * iA[j] : dAA[j];
-      if (p.dh0 != nullptr) p.dh0[o] = dh[j];
+    for (int k = 0; k < NP; ++k) {
+      const float2 da = (METHOD == kZOH) ? mul2(dAA[k], iA[k]) : dAA[k];
+      p.part_A[bd + ((2 * k) ^ perm)] = da.x;
+      p.part_A[bd + ((2 * k + 1) ^ perm)] = da.y;
+      if (p.dh0 != nullptr) {
+        p.dh0[bd + ((2 * k) ^ perm)] = dh[k].x;
+        p.dh0[bd + ((2 * k + 1) ^ perm)] = dh[k].y;
+      }
     }
   }
   if (tid < DT && d0 + tid < p.D) {

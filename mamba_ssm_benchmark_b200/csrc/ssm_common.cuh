@@ -84,6 +84,27 @@ __device__ __forceinline__ float rcp(float x) {
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Packed pair arithmetic (FFMA2 / FMUL2 / FADD2 on sm_100): one instruction for two states.
+__device__ __forceinline__ float2 bc2(float x) { return make_float2(x, x); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 ex2x2(float2 x) { return make_float2(ex2(x.x), ex2(x.y)); }
+__device__ __forceinline__ float2 rcpx2(float2 x) { return make_float2(rcp(x.x), rcp(x.y)); }
+// G consecutive values as G/2 pairs
+template <int G, typename T>
+__device__ __forceinline__ void loadp(const T* p, float2 (&o)[G / 2]) {
+  float v[G];
+  loadg<G>(p, v);
+#pragma unroll
+  for (int i = 0; i < G / 2; ++i) o[i] = make_float2(v[2 * i], v[2 * i + 1]);
+}
+template <int G>
+__device__ __forceinline__ void storep(float* p, const float2 (&v)[G / 2]) {
+  if constexpr (G == 4) *reinterpret_cast<float4*>(p) = make_float4(v[0].x, v[0].y, v[1].x, v[1].y);
+  else *reinterpret_cast<float2*>(p) = v[0];
+}
+
 // logistic sigmoid from e^-z = 2^(-z log2 e)
 __device__ __forceinline__ float sigmoid(float z) { return rcp(1.0f + ex2(-z * kLog2e)); }
 

@@ -13,7 +13,10 @@ static cudaError_t launch_fwd_nm(const FwdParams& p, dim3 grid, cudaStream_t str
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
   }
-  kern<<<grid, Geo<N, G>::NT, smem, stream>>>(p);
+  // one warp per CTA; grid.x counts CPW-channel slices
+  dim3 g2(grid);
+  g2.x = (unsigned)((p.D + Geo<N, G>::CPW - 1) / Geo<N, G>::CPW);
+  kern<<<g2, 32, smem, stream>>>(p);
   return cudaGetLastError();
 }
 
