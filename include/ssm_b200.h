@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define SSM_B200_ABI_VERSION 2
+#define SSM_B200_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define SSM_API __attribute__((visibility("default")))
@@ -128,6 +128,32 @@ SSM_API int ssm_scan_bwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t met
                  ssm_view du, ssm_view ddelta, float* dA, ssm_view dBm, ssm_view dCm,
                  float* dDskip, ssm_view dz, float* dh0,
                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Backward scan without a caller workspace.  No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory when they run the backward — a process
+ * whose memory pool is fixed after start-up and forbids cudaMalloc on the hot path, or a
+ * plugin whose host application owns all device memory and gives it no allocator.
+ *
+ * Same arguments and results as ssm_scan_bwd, minus the workspace: the scratch lives in a
+ * fixed device array inside the library, SSM_NOALLOC_SCRATCH_BYTES (32 MiB) per GPU that
+ * loads the library, held until the process exits.  Shapes whose backward needs more
+ * scratch than that (ssm_scan_bwd_workspace_size) are rejected with SSM_ERR_WORKSPACE and
+ * a message naming both sizes.  The call allocates nothing.
+ *   - The first call on a device looks up the array's device address once for that
+ *     device (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - Every call shares the one array and leaves its contents behind (the backward
+ *     overwrites everything it reads, so nothing needs clearing).  Calls that overlap on
+ *     the GPU — concurrent streams, or several host threads — race on it: serialise them.
+ * ------------------------------------------------------------------------------- */
+#define SSM_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+SSM_API int ssm_scan_bwd_noalloc(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method,
+                         ssm_view u, ssm_view delta, const float* A, ssm_view Bm, ssm_view Cm,
+                         const float* Dskip, ssm_view z, const float* h0,
+                         const float* chunk_states, ssm_view ygate, ssm_view dy, const float* dlast,
+                         ssm_view du, ssm_view ddelta, float* dA, ssm_view dBm, ssm_view dCm,
+                         float* dDskip, ssm_view dz, float* dh0, void* stream);
 
 /* ---------------------------------------------------------------------------------
  * Sequence-parallel forward in two phases (one sequence split over ranks or streams).

@@ -27,6 +27,12 @@ cudaError_t launch_update(int N, bool bf16, const UpdParams& p, cudaStream_t str
 
 using namespace ssm;
 
+namespace ssm {
+// Internal (not exported): lets other translation units set the message ssm_last_error_message
+// returns.
+int report_error(int code, const char* msg);
+}  // namespace ssm
+
 // Device-side error word set by kernels whose bounded waits gave up.
 __device__ int g_ssm_device_error = 0;
 
@@ -339,6 +345,8 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
 }
 
 }  // namespace
+
+int ssm::report_error(int code, const char* msg) { return fail(code, "%s", msg); }
 
 extern "C" {
 
