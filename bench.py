@@ -18,6 +18,10 @@ N > 1  : one process per GPU (torchrun).  Channel sharding, weak scaling: every 
          ends with an NCCL all-reduce of dB|dC (the real exchange of channel sharding).
          A token is one (batch, position) row through 512 channels, so the job processes
          N x B x L tokens per step.
+--config 2 : the long-context forward (B=1, L=131072, D=512): the sequence is split into N
+         contiguous shards (strong scaling); each rank summarises its shard, the summaries are
+         all-gathered over NCCL and composed, and each rank finishes its shard from its
+         carried-in state (mamba_ssm_benchmark_b200/sharding.py).
 --impl reference : the reference's CPU scan (the oracle port of models/scan.py, chunked scan +
          recomputing backward) on the host cores, bounded samples of the same workload.
 """
@@ -46,7 +50,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--config", type=int, choices=(1, 3), default=1)
+    ap.add_argument("--config", type=int, choices=(1, 2, 3), default=1)
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -172,7 +176,7 @@ class ScanStep:
 
 def e2e_run(cfg, device, steps, world, seed):
     """Public API with host buffers: H2D + fwd + bwd + D2H of every output, per step."""
-    from mamba_ssm_benchmark_b200 import selective_scan_fused
+    from mamba_ssm_benchmark_b200 import selective_scan_fused, sharding
     from mamba_ssm_benchmark_b200.workloads import make_inputs
     ins = make_inputs(cfg.B, cfg.L, cfg.D, cfg.N, seed=seed, dist="config", dtype=cfg.dtype)
     host = {k: v.pin_memory() for k, v in ins.items() if v is not None}
@@ -186,8 +190,10 @@ def e2e_run(cfg, device, steps, world, seed):
         leaves = [dv[k].requires_grad_() for k in ("u", "delta", "A", "Bm", "Cm", "Dskip", "z")]
         y, last = selective_scan_fused(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4], D=leaves[5],
                                        z=leaves[6])
-        grads = torch.autograd.grad(y, leaves, dv["dy"])
-        res = [y.detach(), last.detach()] + list(grads)
+        grads = list(torch.autograd.grad(y, leaves, dv["dy"]))
+        if world > 1:
+            sharding.reduce_shared_grads(grads[3:5])          # dBm, dCm: partial sums over channel shards
+        res = [y.detach(), last.detach()] + grads
         if outs_host is None:
             outs_host = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
         for o, r in zip(outs_host, res):
@@ -213,7 +219,7 @@ def e2e_run(cfg, device, steps, world, seed):
     return ms / steps, h2d, d2h
 
 
-def cpu_reference_sample(cfg, budget_s, d_slice=None, b_rows=None, repeats_min=3):
+def cpu_reference_sample(cfg, budget_s, d_slice=None, b_rows=None, repeats_min=3, backward=True):
     """Oracle port (the reference's chunked CPU scan + recomputing backward) on a slice of the
     workload; returns (tokens/s in 512-channel token units, description, samples)."""
     from mamba_ssm_benchmark_b200.workloads import make_inputs
@@ -226,7 +232,8 @@ def cpu_reference_sample(cfg, budget_s, d_slice=None, b_rows=None, repeats_min=3
     def one():
         lv = [ins[k].clone().requires_grad_() for k in ("u", "delta", "A", "Bm", "Cm", "Dskip", "z")]
         y, _ = O.selective_scan_fused(lv[0], lv[1], lv[2], lv[3], lv[4], Dskip=lv[5], z=lv[6])
-        torch.autograd.grad(y, lv, ins["dy"])
+        if backward:
+            torch.autograd.grad(y, lv, ins["dy"])
 
     one()
     times = []
@@ -239,7 +246,8 @@ def cpu_reference_sample(cfg, budget_s, d_slice=None, b_rows=None, repeats_min=3
             break
     med = statistics.median(times)
     tokens = b * cfg.L * d / 512.0
-    desc = f"B={b} of {cfg.B} rows, L={cfg.L}, {d} of {cfg.D} channels, N={cfg.N}, fused fwd+bwd; median of {len(times)}"
+    desc = (f"B={b} of {cfg.B} rows, L={cfg.L}, {d} of {cfg.D} channels, N={cfg.N}, fused "
+            f"{'fwd+bwd' if backward else 'fwd'}; median of {len(times)}")
     return tokens / med, desc, times
 
 
@@ -250,7 +258,8 @@ def run_reference(args, cfg, workload):
     # size one "step" so that warmup + steps fit in ~150 s of host time
     from mamba_ssm_benchmark_b200.workloads import make_inputs  # noqa: F401
     budget = 150.0 / max(1, args.steps + args.warmup)
-    probe_rate, _, probe = cpu_reference_sample(cfg, 0.0, d_slice=min(cfg.D, 64), b_rows=1, repeats_min=1)
+    probe_rate, _, probe = cpu_reference_sample(cfg, 0.0, d_slice=min(cfg.D, 64), b_rows=1, repeats_min=1,
+                                                backward=cfg.backward)
     t_probe = statistics.median(probe)
     d_s = int(max(8, min(cfg.D, 64 * budget / max(t_probe, 1e-6))) // 8 * 8)
     b_s = 1
@@ -264,7 +273,8 @@ def run_reference(args, cfg, workload):
     def step():
         lv = [ins[k].clone().requires_grad_() for k in ("u", "delta", "A", "Bm", "Cm", "Dskip", "z")]
         y, _ = O.selective_scan_fused(lv[0], lv[1], lv[2], lv[3], lv[4], Dskip=lv[5], z=lv[6])
-        torch.autograd.grad(y, lv, ins["dy"])
+        if cfg.backward:
+            torch.autograd.grad(y, lv, ins["dy"])
 
     for _ in range(args.warmup):
         step()
@@ -274,17 +284,170 @@ def run_reference(args, cfg, workload):
     dt = time.perf_counter() - t0
     tokens = b_s * cfg.L * d_s / 512.0
     value = tokens * args.steps / dt
-    sample = f"per step: B={b_s} of {cfg.B} rows, L={cfg.L}, {d_s} of {cfg.D} channels, N={cfg.N}, fused fwd+bwd " \
-             f"(tokens counted in 512-channel units)"
+    sample = f"per step: B={b_s} of {cfg.B} rows, L={cfg.L}, {d_s} of {cfg.D} channels, N={cfg.N}, fused " \
+             f"{'fwd+bwd' if cfg.backward else 'fwd'} (tokens counted in 512-channel units)"
     cores = torch.get_num_threads()
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "higher_is_better": True, "scaling": "strong" if args.config == 2 else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
             "config": {"workload": workload, "B": cfg.B, "L": cfg.L, "D": cfg.D, "N": cfg.N},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                              "sample": sample + "; oracle/scan_oracle.py restates models/scan.py (chunked)"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def run_sequence_shards(args, cfg, workload, rank, world, device):
+    """Config 2: one long sequence split into ``world`` contiguous shards (strong scaling).
+
+    Per step and rank: summary pass over the shard, NCCL all-gather of the (decay, hend)
+    summaries, prefix composition, finish pass from the carried-in state.  On one GPU the step
+    is a single ssm_scan_fwd over the whole sequence (which splits it into segments itself)."""
+    from mamba_ssm_benchmark_b200 import _native as nat
+    from mamba_ssm_benchmark_b200 import selective_scan_fused, sharding
+    from mamba_ssm_benchmark_b200.workloads import algorithmic_bytes, make_inputs
+    lo, hi = sharding.shard_range(cfg.L, world, rank)
+    Ls = hi - lo
+    B, D, N = cfg.B, cfg.D, cfg.N
+    sets = 1 if world == 1 else 2        # at 8 shards one set is ~130 MB: rotate two to stay above L2
+    stream = torch.cuda.current_stream(device)
+    lib = nat.lib()
+    data = []
+    for s_ in range(sets):
+        ins = make_inputs(B, Ls, D, N, seed=100 * s_ + rank, dist="config", dtype=cfg.dtype, device=device)
+        data.append(ins)
+    if world == 1:
+        outs = [(torch.empty(B, Ls, D, dtype=cfg.dtype, device=device),
+                 torch.empty(B, D, N, dtype=torch.float32, device=device)) for _ in range(sets)]
+        wsb = nat.fwd_workspace_bytes(B, Ls, D, N)
+        ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=device)
+        launches = 1 if wsb == 0 else 3
+
+        def step(i, ev=None):
+            d, (y, last) = data[i % sets], outs[i % sets]
+            if ev is not None:
+                ev[0].record(stream)
+            rc = lib.ssm_scan_fwd(B, Ls, D, N, 0, nat.view3(d["u"]), nat.view3(d["delta"]), nat.ptr(d["A"]),
+                                  nat.view3(d["Bm"]), nat.view3(d["Cm"]), nat.ptr(d["Dskip"]), nat.view3(d["z"]),
+                                  None, nat.view3(y), nat.NULL_VIEW, nat.ptr(last), None, ws.data_ptr(), wsb,
+                                  nat.stream_of(device))
+            nat.check(rc, "ssm_scan_fwd")
+            if ev is not None:
+                ev[1].record(stream)
+    else:
+        shards = [sharding.SequenceShard(d["u"], d["delta"], d["A"], d["Bm"], d["Cm"], "zoh", D=d["Dskip"], z=d["z"])
+                  for d in data]
+        launches = 2 if shards[0].wsb == 0 else 4
+
+        def step(i, ev=None):
+            sh = shards[i % sets]
+            decay, hend = sh.summary()
+            decays, hends = sharding.exchange_summaries(decay, hend)
+            h_in, _ = sharding.compose_prefix(decays, hends)
+            if ev is not None:
+                ev[0].record(stream)
+            sh.finish(h_in[rank])
+            if ev is not None:
+                ev[1].record(stream)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(device)
+    K = args.steps
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(K):
+        step(i, kev[i])
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    k_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    if world > 1:
+        t = torch.tensor([ms, k_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, k_ms = t.tolist()
+    ms_step = ms / K
+    tokens_step = B * cfg.L
+    value = tokens_step / (ms_step / 1e3)
+    eb = 4 if cfg.dtype == torch.float32 else 2
+    fwd_bytes, _ = algorithmic_bytes(B, Ls, D, N, eb, fused=True, backward=False)
+    peak, peak_kind = measured_peak()
+    achieved = fwd_bytes / (k_ms / 1e3) / 1e9
+
+    # e2e: public API with this rank's shard in pinned host memory
+    host = {k: data[0][k].cpu().pin_memory() for k in ("u", "delta", "A", "Bm", "Cm", "Dskip", "z")}
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    y_host = torch.empty(B, Ls, D, dtype=cfg.dtype, pin_memory=True)
+    last_host = torch.empty(B, D, N, dtype=torch.float32, pin_memory=True)
+    d2h = y_host.numel() * y_host.element_size() + last_host.numel() * 4
+
+    def e2e_step():
+        dv = {k: v.to(device, non_blocking=True) for k, v in host.items()}
+        scan = sharding.sequence_sharded_scan if world > 1 else selective_scan_fused
+        y, last = scan(dv["u"], dv["delta"], dv["A"], dv["Bm"], dv["Cm"], D=dv["Dskip"], z=dv["z"])
+        y_host.copy_(y, non_blocking=True)
+        last_host.copy_(last, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    a1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = a0.elapsed_time(a1) / args.e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = t.item()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, desc, _ = cpu_reference_sample(cfg, budget_s=12.0, b_rows=1, d_slice=16, backward=False)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": desc + "; tokens counted in 512-channel units; oracle/scan_oracle.py restates "
+                                "models/scan.py (chunked scan)"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": workload, "B": B, "L": cfg.L, "L_per_gpu": Ls, "D": D, "N": N,
+                       "activations": str(cfg.dtype).replace("torch.", ""), "fused_gate": True,
+                       "parallelism": f"sequence-sharded x{world} (strong)" if world > 1 else "single GPU",
+                       "l2": f"{sets} rotating input set(s), inputs > 126 MB L2",
+                       "token": "one (batch, position) row through 512 channels"},
+            "roofline": {"kernel": "ssm_scan_fwd" if world == 1 else "ssm_scan_fwd_finish", "bound": "hbm",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6.65 TB/s", "traffic": None,
+                         "algorithmic_bytes_per_launch": fwd_bytes, "avg_launch_ms": k_ms},
+            "e2e": {"value": tokens_step / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": args.e2e_steps},
+            "gpu_launches": K * launches,
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
+                       "samples": clk["samples"]},
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
 
 
 def main():
@@ -302,6 +465,10 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=device)
+    if args.config == 2:
+        run_sequence_shards(args, cfg, workload, rank, world, device)
+        return
+    from mamba_ssm_benchmark_b200 import sharding
     sets = 4 if args.config == 1 else 1
     steps = [ScanStep(cfg, device, seed=1000 * s + rank, shared_seed=1000 * s) for s in range(sets)]
     stream = torch.cuda.current_stream(device)
@@ -316,7 +483,7 @@ def main():
         if ev is not None:
             ev[1].record(stream)
         if world > 1:
-            torch.distributed.all_reduce(dBC_bufs[i % sets])
+            sharding.reduce_shared_grads([dBC_bufs[i % sets]])
 
     for i in range(args.warmup):
         one(i)

@@ -1,0 +1,83 @@
+"""GPU parity of the sharded scan (mamba_ssm_benchmark_b200/sharding.py).
+
+On one GPU the sequence-shard protocol is emulated shard by shard with the package's own
+summary / compose / finish functions; with two or more GPUs the NCCL rank program
+(tests/sharding_nccl_worker.py) runs under torchrun.
+"""
+
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+from mamba_ssm_benchmark_b200 import _native as nat
+from mamba_ssm_benchmark_b200 import selective_scan_fused, sharding
+from mamba_ssm_benchmark_b200.workloads import make_inputs
+from oracle import scan_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(autouse=True)
+def _no_device_errors():
+    yield
+    assert nat.read_device_error() == 0
+
+
+@pytest.mark.parametrize("shards", [1, 2, 5])
+@pytest.mark.parametrize("method", ["zoh", "euler", "bilinear"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_sequence_shards_single_gpu(shards, method, dtype):
+    """summary of every shard -> compose_prefix -> finish every shard == one call over the whole
+    sequence, and == the oracle."""
+    B, L, D, N = 2, 3000, 96, 16
+    ins = make_inputs(B, L, D, N, seed=shards, dist="config", h0=True, dtype=dtype)
+    dev = {k: (v.to(DEV) if v is not None else None) for k, v in ins.items()}
+    u, dl, A, Bm, Cm, Dk, z, h0 = (dev[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dskip", "z", "h0"))
+    bounds = [sharding.shard_range(L, shards, r) for r in range(shards)]
+    pieces = [sharding.SequenceShard(u[:, lo:hi], dl[:, lo:hi], A, Bm[:, lo:hi], Cm[:, lo:hi], method, D=Dk,
+                                     z=z[:, lo:hi]) for lo, hi in bounds]
+    sums = [p.summary() for p in pieces]
+    decays = torch.stack([s[0] for s in sums])
+    hends = torch.stack([s[1] for s in sums])
+    h_in, last = sharding.compose_prefix(decays, hends, h0)
+    ys = []
+    for r, (lo, hi) in enumerate(bounds):
+        y, lst = pieces[r].finish(h_in[r])
+        assert y.dtype == dtype
+        want_last = h_in[r + 1] if r + 1 < shards else last
+        assert O.normwise_error(lst, want_last) < 1e-5
+        ys.append(y)
+    y = torch.cat(ys, 1)
+    y_one, last_one = selective_scan_fused(u, dl, A, Bm, Cm, h0=h0, method=method, D=Dk, z=z)
+    assert O.normwise_error(y, y_one) < 1e-5
+    assert O.normwise_error(last, last_one) < 1e-5
+    y_ref, last_ref = O.selective_scan_fused(*(ins[k].float() for k in ("u", "delta", "A", "Bm", "Cm")),
+                                             h0=ins["h0"], method=method, Dskip=ins["Dskip"], z=ins["z"].float())
+    tol = 1e-4 if dtype == torch.float32 else 1e-2
+    assert O.normwise_error(y.float().cpu(), y_ref) < tol
+    assert O.normwise_error(last.cpu(), last_ref) < (1e-4 if dtype == torch.float32 else 1e-3)
+
+
+def test_sequence_sharded_scan_without_process_group():
+    """Outside torch.distributed the sharded scan is the whole-sequence scan."""
+    B, L, D, N = 1, 1024, 64, 16
+    ins = make_inputs(B, L, D, N, seed=4, dist="config", device=DEV)
+    args = [ins[k] for k in ("u", "delta", "A", "Bm", "Cm")]
+    y, last = sharding.sequence_sharded_scan(*args, D=ins["Dskip"], z=ins["z"])
+    y1, last1 = selective_scan_fused(*args, D=ins["Dskip"], z=ins["z"])
+    assert O.normwise_error(y, y1) < 1e-6
+    assert O.normwise_error(last, last1) < 1e-6
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sharding_over_nccl_two_ranks():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MASTER_ADDR="127.0.0.1")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29541", os.path.join(ROOT, "tests", "sharding_nccl_worker.py")]
+    res = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
