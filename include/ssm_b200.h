@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define SSM_B200_ABI_VERSION 3
+#define SSM_B200_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define SSM_API __attribute__((visibility("default")))
@@ -177,6 +177,27 @@ SSM_API int ssm_scan_fwd_finish(int64_t B, int64_t L, int64_t D, int64_t N, int3
                         const float* Dskip, ssm_view z, const float* h_in,
                         ssm_view y, ssm_view ygate, float* last, float* chunk_states,
                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Sequence-parallel backward, phase 1: the adjoint summary of this shard.  The
+ * backward of a sequence split over shards needs, on every shard, the adjoint dlast
+ * entering it from the right; that is the gradient with respect to the next shard's
+ * initial state, which is affine in the next shard's own dlast:
+ *   dstart(dlast) = dstart(0) + decay * dlast      (elementwise over (B, D, N))
+ * This call returns dstart(0) -- the reverse adjoint dh_{t-1} = a_t (dh_t + C_t dys_t),
+ * dys = dy * silu(z) (dy when z is NULL), run over the shard from a zero adjoint at its
+ * end -- and decay = prod_t a_t over the shard.  Composing the shards' summaries from
+ * the last shard to the first gives each shard's dlast; ssm_scan_bwd with that dlast
+ * and h0 = the shard's carried-in state finishes the shard.  The reverse adjoint is
+ * models/scan.py:239-240 (kernels/triton_scan.py:187, 223); the split across shards is
+ * the reverse counterpart of the two-level scan's chunk combine (models/scan.py:160-164).
+ * delta, z, dy: (B, L, D); Cm: (B, L, N); A: (D, N) fp32; decay, dstart: (B, D, N) fp32
+ * outputs.  Workspace: ssm_scan_fwd_workspace_size bytes.
+ * ------------------------------------------------------------------------------- */
+SSM_API int ssm_scan_bwd_summary(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method,
+                         ssm_view delta, const float* A, ssm_view Cm, ssm_view z, ssm_view dy,
+                         float* decay, float* dstart,
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------
  * Single-token state update (decode).  The reference has no function for this; its

@@ -17,13 +17,14 @@ SSM_OK, SSM_ERR_INVALID, SSM_ERR_DTYPE, SSM_ERR_WORKSPACE, SSM_ERR_CUDA, SSM_ERR
 SSM_F32, SSM_BF16 = 0, 1
 METHODS = {"zoh": 0, "euler": 1, "bilinear": 2}
 DTYPES = {torch.float32: SSM_F32, torch.bfloat16: SSM_BF16}
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 # Every symbol include/ssm_b200.h declares (checked by the tests).
 EXPORTED = (
     "ssm_abi_version", "ssm_last_error_message", "ssm_read_device_error",
     "ssm_scan_fwd_workspace_size", "ssm_scan_fwd", "ssm_scan_bwd_workspace_size", "ssm_scan_bwd",
     "ssm_scan_fwd_summary", "ssm_scan_fwd_finish", "ssm_state_update", "ssm_scan_bwd_noalloc",
+    "ssm_scan_bwd_summary",
 )
 
 
@@ -58,6 +59,8 @@ _SIGNATURES = {
     "ssm_scan_bwd": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _V, _P, _V, _V, _P, _V, _P,
                                     _P, _V, _V, _P, _V, _V, _P, _V, _V, _P, _V, _P, _P, _SZ, _P]),
     "ssm_state_update": (ctypes.c_int, [_I64, _I64, _I64, _I32, _P, _V, _V, _P, _V, _V, _P, _V, _V, _P]),
+    "ssm_scan_bwd_summary": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _P, _V, _V, _V, _P, _P, _P, _SZ,
+                                            _P]),
     "ssm_scan_bwd_noalloc": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _V, _P, _V, _V, _P, _V, _P,
                                             _P, _V, _V, _P, _V, _V, _P, _V, _V, _P, _V, _P, _P]),
 }

@@ -151,16 +151,22 @@ int choose_g(int64_t B, int64_t D, int64_t N) {
   return 4;
 }
 
-// Sequence split of the forward: S segments of seg_len steps (a multiple of 16).  Splitting
-// doubles the recurrence work (summary pass + main pass), so it is used only when the
-// (batch x channel-tile) grid alone cannot give every SM a CTA.
-void plan_segments(int64_t B, int64_t L, int64_t D, int* nseg, int* seg_len) {
-  const int64_t ndt = (D + 31) / 32;
-  const int64_t ncta = ndt * B;
+// Sequence split of the forward: S segments of seg_len steps (a multiple of 16).  The forward runs one warp per (batch, CPW channels); when that
+// is fewer than two warps per SM (long sequences over few channels: B = 1, D = 512 gives 64
+// warps) the sequence is cut into S segments of at least 8 chunks, aiming at 64 warps' worth of
+// work per SM (several waves: shorter segments balance better).  A split costs one extra pass
+// without outputs (measured on config-1 shapes: S = 2 is 35 % slower than S = 1), so shapes with
+// enough warps are not split.  (B = 1, L = 131072, D = 512: S = 148 takes 0.90 ms, S = 19 1.28 ms.)
+void plan_segments(int64_t B, int64_t L, int64_t D, int64_t N, int* nseg, int* seg_len) {
+  const int64_t cpw = 32 * choose_g(B, D, N) / N;
+  const int64_t warps = B * ((D + cpw - 1) / cpw);
   const int64_t nchunk = (L + kChunk - 1) / kChunk;
   const int64_t sms = sm_count();
   int64_t S = 1;
-  if (ncta < sms && nchunk >= 4) S = std::min<int64_t>((2 * sms + ncta - 1) / ncta, nchunk / 2);
+  if (warps < 2 * sms && nchunk >= 16) S = std::min<int64_t>((64 * sms + warps - 1) / warps, nchunk / 8);
+#ifdef SSM_FWD_SEGS_FORCE
+  S = std::min<int64_t>(SSM_FWD_SEGS_FORCE, nchunk);
+#endif
   if (S < 1) S = 1;
   int64_t len = ((L + S - 1) / S + kChunk - 1) / kChunk * kChunk;
   S = (L + len - 1) / len;
@@ -170,7 +176,7 @@ void plan_segments(int64_t B, int64_t L, int64_t D, int* nseg, int* seg_len) {
 
 size_t fwd_ws_bytes(int64_t B, int64_t L, int64_t D, int64_t N) {
   int S, len;
-  plan_segments(B, L, D, &S, &len);
+  plan_segments(B, L, D, N, &S, &len);
   if (S <= 1) return 0;
   return 3 * (size_t)B * S * D * N * sizeof(float) + 256;
 }
@@ -219,7 +225,8 @@ int check_f32(const char* name, const void* p, bool required) {
 
 // Shared body of ssm_scan_fwd / ssm_scan_fwd_finish / ssm_scan_fwd_summary.
 // phase: 0 = full forward, 1 = summary only (writes decay/hend), 2 = finish (reuses the
-// per-segment summaries a phase-1 call left in the workspace).
+// per-segment summaries a phase-1 call left in the workspace), 3 = adjoint summary (u carries
+// dy and Bm carries C; writes decay and the adjoint at the sequence start into decay/hend).
 int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm_view u, ssm_view delta,
              const float* A, ssm_view Bm, ssm_view Cm, const float* Dskip, ssm_view z, const float* h0,
              ssm_view y, ssm_view ygate, float* last, float* chunk_states, float* tot_decay, float* tot_hend,
@@ -231,7 +238,9 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   if (dt != SSM_F32 && dt != SSM_BF16) return fail(SSM_ERR_DTYPE, "u dtype %d unsupported", dt);
   if ((rc = check_view("delta", delta, dt, D, true))) return rc;
   if ((rc = check_view("Bm", Bm, dt, N, true))) return rc;
-  if (phase != 1) {
+  const bool summary = (phase == 1 || phase == 3);
+  if (phase == 3 && (rc = check_view("z", z, dt, D, false))) return rc;
+  if (!summary) {
     if ((rc = check_view("Cm", Cm, dt, N, true))) return rc;
     if ((rc = check_view("z", z, dt, D, false))) return rc;
     if ((rc = check_view("y", y, dt, D, true))) return rc;
@@ -242,8 +251,8 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   if ((rc = check_f32("h0", h0, false))) return rc;
   if ((rc = check_f32("last", last, false))) return rc;
   if ((rc = check_f32("chunk_states", chunk_states, false))) return rc;
-  if (phase == 1 && (tot_decay == nullptr || tot_hend == nullptr || !aligned16(tot_decay) || !aligned16(tot_hend)))
-    return fail(SSM_ERR_INVALID, "decay and hend outputs are required and must be 16-byte aligned");
+  if (summary && (tot_decay == nullptr || tot_hend == nullptr || !aligned16(tot_decay) || !aligned16(tot_hend)))
+    return fail(SSM_ERR_INVALID, "the two summary outputs are required and must be 16-byte aligned");
   const size_t need = fwd_ws_bytes(B, L, D, N);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need))
     return fail(SSM_ERR_WORKSPACE, "forward workspace of %zu bytes required, %zu given", need, workspace_bytes);
@@ -258,7 +267,7 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   p.Cm = dact(Cm);
   p.y = dact(y);
   p.yg = dact(ygate);
-  p.save_ygate = (phase != 1 && ygate.ptr != nullptr) ? 1 : 0;
+  p.save_ygate = (!summary && ygate.ptr != nullptr) ? 1 : 0;
   p.A = A;
   p.Dskip = Dskip;
   p.last = last;
@@ -275,20 +284,19 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   const int cpw = (int)(32 * G / N);
   const int bxc = std::max<int>(cpw, (int)(16 / esize(dt)));
   bool use_tma = tma_ok(u, B, L, D) && tma_ok(delta, B, L, D) && tma_ok(Bm, B, L, N);
-  if (phase != 1) use_tma = use_tma && tma_ok(Cm, B, L, N) && (!p.has_z || tma_ok(z, B, L, D));
+  if (!summary) use_tma = use_tma && tma_ok(Cm, B, L, N);
+  if (phase != 1) use_tma = use_tma && (!p.has_z || tma_ok(z, B, L, D));
   if (use_tma) {
     bool ok = make_map(&p.tm_u, u, B, L, D, bxc, kChunk) && make_map(&p.tm_dt, delta, B, L, D, bxc, kChunk) &&
               make_map(&p.tm_B, Bm, B, L, N, (int)N, kChunk);
-    if (phase != 1) {
-      ok = ok && make_map(&p.tm_C, Cm, B, L, N, (int)N, kChunk);
-      if (p.has_z) ok = ok && make_map(&p.tm_z, z, B, L, D, bxc, kChunk);
-    }
+    if (!summary) ok = ok && make_map(&p.tm_C, Cm, B, L, N, (int)N, kChunk);
+    if (phase != 1 && p.has_z) ok = ok && make_map(&p.tm_z, z, B, L, D, bxc, kChunk);
     use_tma = ok;
   }
   p.use_tma = use_tma ? 1 : 0;
 
   int S, len;
-  plan_segments(B, L, D, &S, &len);
+  plan_segments(B, L, D, N, &S, &len);
   p.nseg = S;
   p.seg_len = len;
   const unsigned ndt = (unsigned)((D + 31) / 32);
@@ -300,12 +308,13 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   };
   cudaError_t e;
 
+  const int smode = (phase == 3) ? kModeAdjoint : kModeSummary;
   if (S == 1) {
-    if (phase == 1) {
+    if (summary) {
       FwdParams q = p;
       q.seg_hend = tot_hend;
       q.seg_decay = tot_decay;
-      if ((e = launch(kModeSummary, q)) != cudaSuccess) return cuda_fail(e, "forward summary launch");
+      if ((e = launch(smode, q)) != cudaSuccess) return cuda_fail(e, "summary launch");
       return SSM_OK;
     }
     p.h_init = h0;
@@ -323,22 +332,23 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
     FwdParams q = p;
     q.seg_hend = seg_hend;
     q.seg_decay = seg_decay;
-    if ((e = launch(kModeSummary, q)) != cudaSuccess) return cuda_fail(e, "forward summary launch");
+    if ((e = launch(smode, q)) != cudaSuccess) return cuda_fail(e, "summary launch");
   }
   CarryParams cp;
   memset(&cp, 0, sizeof(cp));
-  cp.h_init = (phase == 1) ? nullptr : h0;
+  cp.h_init = summary ? nullptr : h0;
   cp.seg_decay = seg_decay;
   cp.seg_hend = seg_hend;
-  cp.seg_init = (phase == 1) ? nullptr : seg_init;
-  cp.tot_decay = (phase == 1) ? tot_decay : nullptr;
-  cp.tot_hend = (phase == 1) ? tot_hend : nullptr;
+  cp.seg_init = summary ? nullptr : seg_init;
+  cp.tot_decay = summary ? tot_decay : nullptr;
+  cp.tot_hend = summary ? tot_hend : nullptr;
   cp.B = (int)B;
   cp.D = (int)D;
   cp.N = (int)N;
   cp.nseg = S;
+  cp.reverse = (phase == 3) ? 1 : 0;
   if ((e = launch_carry(cp, stream)) != cudaSuccess) return cuda_fail(e, "carry launch");
-  if (phase == 1) return SSM_OK;
+  if (summary) return SSM_OK;
   p.seg_init = seg_init;
   if ((e = launch(kModeMain, p)) != cudaSuccess) return cuda_fail(e, "forward launch");
   return SSM_OK;
@@ -399,6 +409,17 @@ int ssm_scan_fwd_summary(int64_t B, int64_t L, int64_t D, int64_t N, int32_t met
   none.dtype = u.dtype;
   return fwd_impl(1, B, L, D, N, method, u, delta, A, Bm, none, nullptr, none, nullptr, none, none, nullptr,
                   nullptr, decay, hend, workspace, workspace_bytes, stream);
+}
+
+int ssm_scan_bwd_summary(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm_view delta,
+                         const float* A, ssm_view Cm, ssm_view z, ssm_view dy, float* decay, float* dstart,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (dy.ptr == nullptr) return fail(SSM_ERR_INVALID, "dy is required");
+  ssm_view none;
+  memset(&none, 0, sizeof(none));
+  none.dtype = dy.dtype;
+  return fwd_impl(3, B, L, D, N, method, dy, delta, A, Cm, none, nullptr, z, nullptr, none, none, nullptr,
+                  nullptr, decay, dstart, workspace, workspace_bytes, stream);
 }
 
 int ssm_scan_fwd_finish(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm_view u, ssm_view delta,

@@ -506,18 +506,46 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
 // each in a fixed order, and writes dB, dC (element type T), dA, dD (fp32).
 template <typename T>
 __global__ void ssm_bwd_finalize(const FinParams p) {
+  // Each sum is taken in index order; the loads of a group of kU terms are issued together
+  // (they are independent), then added in order, so the result does not depend on kU.
+  constexpr int kU = 8;
   const long long n2 = 2LL * p.N;
   const long long nbc = (long long)p.B * p.L * n2;
   const long long nA = (long long)p.D * p.N;
   const long long total = nbc + nA + (p.dD != nullptr ? p.D : 0);
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
        idx += (long long)gridDim.x * blockDim.x) {
+    const float* src;
+    long long stride;
+    int cnt;
     if (idx < nbc) {
       const int v = (int)(idx % n2);
       const long long bt = idx / n2;
       const int t = (int)(bt % p.L), b = (int)(bt / p.L);
-      float s = 0.f;
-      for (int q = 0; q < p.ndt; ++q) s += p.part_bc[(((size_t)b * p.ndt + q) * p.L + t) * n2 + v];
+      src = p.part_bc + ((size_t)b * p.ndt * p.L + t) * n2 + v;
+      stride = (long long)p.L * n2;
+      cnt = p.ndt;
+    } else if (idx < nbc + nA) {
+      src = p.part_A + (idx - nbc);
+      stride = nA;
+      cnt = p.B;
+    } else {
+      src = p.part_D + (idx - nbc - nA);
+      stride = p.D;
+      cnt = p.B;
+    }
+    float s = 0.f;
+    for (int q0 = 0; q0 < cnt; q0 += kU) {
+      float v[kU];
+#pragma unroll
+      for (int k = 0; k < kU; ++k) v[k] = (q0 + k < cnt) ? __ldg(src + (q0 + k) * stride) : 0.f;
+#pragma unroll
+      for (int k = 0; k < kU; ++k) s += v[k];
+    }
+    if (idx < nbc) {
+      const int v = (int)(idx % n2);
+      const long long bt = idx / n2;
+      const int t = (int)(bt % p.L), b = (int)(bt / p.L);
       if (v < p.N) {
         static_cast<T*>(const_cast<void*>(p.dB.ptr))[b * p.dB.sb + (long long)t * p.dB.sl + v] = from_f32<T>(s);
       } else {
@@ -525,15 +553,9 @@ __global__ void ssm_bwd_finalize(const FinParams p) {
             from_f32<T>(s);
       }
     } else if (idx < nbc + nA) {
-      const long long i = idx - nbc;
-      float s = 0.f;
-      for (int b = 0; b < p.B; ++b) s += p.part_A[(size_t)b * nA + i];
-      p.dA[i] = s;
+      p.dA[idx - nbc] = s;
     } else {
-      const long long dd = idx - nbc - nA;
-      float s = 0.f;
-      for (int b = 0; b < p.B; ++b) s += p.part_D[(size_t)b * p.D + dd];
-      p.dD[dd] = s;
+      p.dD[idx - nbc - nA] = s;
     }
   }
 }

@@ -307,6 +307,7 @@ struct CarryParams {
   float* tot_decay;          // (B, D, N) or null
   float* tot_hend;           // (B, D, N) or null
   int B, D, N, nseg;
+  int reverse;               // compose from the last segment to the first (adjoint summaries)
 };
 
 struct UpdParams {

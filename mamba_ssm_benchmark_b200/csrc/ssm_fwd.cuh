@@ -21,7 +21,12 @@
 
 namespace ssm {
 
-enum { kModeMain = 0, kModeSummary = 1 };
+// kModeMain: the forward.  kModeSummary: decay product and end state of a segment scanned from
+// zero (no outputs).  kModeAdjoint: the reverse adjoint of a segment from a zero adjoint at its
+// end, dh_{t-1} = a_t (dh_t + C_t dys_t), giving the gradient with respect to the state entering
+// the segment and the decay product (the backward's counterpart of kModeSummary; the u slot
+// carries dy, the B slot carries C).
+enum { kModeMain = 0, kModeSummary = 1, kModeAdjoint = 2 };
 
 // One warp per CTA.  The CTA owns the CPW channels of one warp; its TMA boxes are BXC channels
 // wide (BXC = CPW, widened to 16 bytes of channels when CPW is narrower: the box then starts at
@@ -72,20 +77,22 @@ __device__ __forceinline__ float2 fwd_apply2(float2 h, float2 a, float2 bco) {
 #ifndef SSM_FWD_SUB
 #define SSM_FWD_SUB 4   // steps per state-independent sub-tile (divides 16)
 #endif
+#ifndef SSM_FWD_GMAJOR
+#define SSM_FWD_GMAJOR 1   // lane = g * CPW + c (state group major) instead of c * LPC + g
+#endif
 
 template <typename S, int MODE>
 __device__ __forceinline__ void fwd_issue_loads(const FwdParams& p, unsigned char* st, uint64_t* bar, int x0,
                                                 int t0, int b) {
-  const bool load_zc = (MODE == kModeMain);
-  const uint32_t tx = 2 * S::ACT + S::BC + (load_zc ? (S::BC + (p.has_z ? S::ACT : 0)) : 0);
+  const bool load_c = (MODE == kModeMain);
+  const bool load_z = (MODE != kModeSummary) && p.has_z;
+  const uint32_t tx = 2 * S::ACT + S::BC + (load_c ? S::BC : 0) + (load_z ? S::ACT : 0);
   mbar_arrive_expect_tx(bar, tx);
   tma_load_3d(st + S::OFF_U, &p.tm_u, bar, x0, t0, b);
   tma_load_3d(st + S::OFF_DT, &p.tm_dt, bar, x0, t0, b);
   tma_load_3d(st + S::OFF_B, &p.tm_B, bar, 0, t0, b);
-  if (load_zc) {
-    tma_load_3d(st + S::OFF_C, &p.tm_C, bar, 0, t0, b);
-    if (p.has_z) tma_load_3d(st + S::OFF_Z, &p.tm_z, bar, x0, t0, b);
-  }
+  if (load_c) tma_load_3d(st + S::OFF_C, &p.tm_C, bar, 0, t0, b);
+  if (load_z) tma_load_3d(st + S::OFF_Z, &p.tm_z, bar, x0, t0, b);
 }
 
 // Plain (non-TMA) box load with zero fill by the warp, for views TMA cannot describe.
@@ -100,7 +107,7 @@ __device__ __forceinline__ void fwd_warp_load(const FwdParams& p, unsigned char*
     auto ld = [&](const DAct& a) { return ok ? static_cast<const T*>(a.ptr)[b * a.sb + tl * a.sl + dg] : zero; };
     reinterpret_cast<T*>(st + S::OFF_U)[e] = ld(p.u);
     reinterpret_cast<T*>(st + S::OFF_DT)[e] = ld(p.dt);
-    if (MODE == kModeMain && p.has_z) reinterpret_cast<T*>(st + S::OFF_Z)[e] = ld(p.z);
+    if (MODE != kModeSummary && p.has_z) reinterpret_cast<T*>(st + S::OFF_Z)[e] = ld(p.z);
   }
   for (int e = threadIdx.x; e < S::TC * N; e += 32) {
     const int tt = e / N, n = e % N;
@@ -128,8 +135,12 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
 
+  // Lane layout: state group major.  The 8 lanes of a quarter warp then share one state group,
+  // so the vector loads of B and C read one address per quarter warp (a broadcast) instead of
+  // LPC different ones.
   const int lane = threadIdx.x;
-  const int c = lane / LPC, g = lane % LPC;
+  const int c = SSM_FWD_GMAJOR ? lane % CPW : lane / LPC, g = SSM_FWD_GMAJOR ? lane / CPW : lane % LPC;
+  constexpr int GSTRIDE = SSM_FWD_GMAJOR ? CPW : 1;   // lane distance between a channel's state groups
   const int b = blockIdx.z, seg = blockIdx.y;
   const int d0 = blockIdx.x * CPW;
   const int x0 = (d0 / BXC) * BXC, dl = d0 - x0 + c;   // box origin and this lane's column
@@ -139,6 +150,8 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
   const int t_begin = seg * p.seg_len;
   const int t_end = min(p.L, t_begin + p.seg_len);
   const int nblk = (t_end - t_begin + TC - 1) / TC;
+  // the adjoint walks the segment's boxes from the last to the first
+  auto blk_t0 = [&](int ib) { return t_begin + ((MODE == kModeAdjoint) ? nblk - 1 - ib : ib) * TC; };
 
   // Per-state constants, as pairs: A, A log2(e) (for 2^x), -1/A.  Channels past D get A = -1
   // and zero inputs.
@@ -164,7 +177,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
     h[i] = bc2(0.f);
     P[i] = bc2(1.f);
   }
-  if (dvalid) {
+  if (dvalid && MODE != kModeAdjoint) {
     const float* src = nullptr;
     if (p.seg_init != nullptr) src = p.seg_init + (((size_t)b * p.nseg + seg) * p.D + d) * N + nbase;
     else if (seg == 0 && p.h_init != nullptr) src = p.h_init + ((size_t)b * p.D + d) * N + nbase;
@@ -181,7 +194,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
       for (int s = 0; s < S::NSTAGE; ++s) mbar_init(&bars[s], 1);
       fence_mbar_init();
       for (int s = 0; s < S::NSTAGE && s < nblk; ++s)
-        fwd_issue_loads<S, MODE>(p, smem + s * S::STAGE, &bars[s], x0, t_begin + s * TC, b);
+        fwd_issue_loads<S, MODE>(p, smem + s * S::STAGE, &bars[s], x0, blk_t0(s), b);
     }
     __syncwarp();
   }
@@ -191,7 +204,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
 
   for (int ib = 0; ib < nblk; ++ib) {
     const int s = ib % S::NSTAGE;
-    const int t0 = t_begin + ib * TC;
+    const int t0 = blk_t0(ib);
     unsigned char* st = smem + s * S::STAGE;
     if (p.use_tma) {
       mbar_wait(&bars[s], (uint32_t)((ib / S::NSTAGE) & 1), p.err);
@@ -209,55 +222,90 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
     if (MODE == kModeMain && p.chunk_states != nullptr && dvalid)   // state entering chunk t0 / 16
       storep<G>(p.chunk_states + (((size_t)b * p.nchunks + t0 / TC) * p.D + d) * N + nbase, h);
 
-    // 16 steps.  The lane's partial y (its G states, plus D u on lane 0 of the group) stays
-    // in registers, stored at yp[(t % LPC) YPL + t / LPC] so that after the reduction lane g
-    // holds steps g, g + LPC, ...; the lane also keeps z of those steps.  Steps are processed
-    // in sub-tiles: phase A computes what does not depend on the state (decays, inputs, C),
-    // phase B is only the recurrence and the y accumulation.
-    float yp[TC], zk[YPL];
+    float yp[TC], zk[YPL];   // main mode: partial y and the gate's z (see below)
+    if constexpr (MODE == kModeAdjoint) {
+      // reverse through the box: dh <- a_t dh + a_t C_t dys_t, dys = dy silu(z) (or dy)
 #pragma unroll
-    for (int t0s = 0; t0s < TC; t0s += SSM_FWD_SUB) {
-      float2 av[SSM_FWD_SUB][NP], bv[SSM_FWD_SUB][NP], cv[SSM_FWD_SUB][NP];
-      float yd[SSM_FWD_SUB];
+      for (int t0s = TC - SSM_FWD_SUB; t0s >= 0; t0s -= SSM_FWD_SUB) {
+        float2 av[SSM_FWD_SUB][NP], cd[SSM_FWD_SUB][NP];
 #pragma unroll
-      for (int q = 0; q < SSM_FWD_SUB; ++q) {
-        const int tt = t0s + q;
-        const float uu = to_f32(Xs[tt * BXC + dl]);
-        const float dtv = to_f32(DLs[tt * BXC + dl]);
-        const float2 u2 = bc2(uu), dt2 = bc2(dtv), dtu2 = bc2(dtv * uu);
-        float2 Bn[NP];
-        loadp<G>(Bs + tt * N + nbase, Bn);
-        if (MODE == kModeMain) loadp<G>(Cs + tt * N + nbase, cv[q]);
-        yd[q] = Dd0 * uu;
+        for (int q = 0; q < SSM_FWD_SUB; ++q) {
+          const int tt = t0s + q;
+          float dys = to_f32(Xs[tt * BXC + dl]);
+          const float dtv = to_f32(DLs[tt * BXC + dl]);
+          if (p.has_z) {
+            const float zz = to_f32(Zs[tt * BXC + dl]);
+            dys *= zz * sigmoid(zz);
+          }
+          const float2 dt2 = bc2(dtv), dys2 = bc2(dys);
+          float2 Cn[NP];
+          loadp<G>(Bs + tt * N + nbase, Cn);
 #pragma unroll
-        for (int i = 0; i < NP; ++i)
-          fwd_coeffs2<METHOD>(dt2, u2, dtu2, Bn[i], Ak[i], A2[i], niA[i], av[q][i], bv[q][i]);
-        if (MODE == kModeMain) {   // branch-free: without z the tiles hold zeros
-          const float zz = to_f32(Zs[tt * BXC + dl]);
-          if (g == tt % LPC) zk[tt / LPC] = zz;
+          for (int i = 0; i < NP; ++i) {
+            float2 unused;
+            fwd_coeffs2<METHOD>(dt2, bc2(0.f), bc2(0.f), Cn[i], Ak[i], A2[i], niA[i], av[q][i], unused);
+            cd[q][i] = mul2(av[q][i], mul2(Cn[i], dys2));
+          }
+        }
+#pragma unroll
+        for (int q = SSM_FWD_SUB - 1; q >= 0; --q) {
+#pragma unroll
+          for (int i = 0; i < NP; ++i) {
+            h[i] = fma2(av[q][i], h[i], cd[q][i]);
+            P[i] = mul2(P[i], av[q][i]);
+          }
         }
       }
+    } else {
+      // 16 steps.  The lane's partial y (its G states, plus D u on lane 0 of the group) stays
+      // in registers, stored at yp[(t % LPC) YPL + t / LPC] so that after the reduction lane g
+      // holds steps g, g + LPC, ...; the lane also keeps z of those steps.  Steps are processed
+      // in sub-tiles: phase A computes what does not depend on the state (decays, inputs, C),
+      // phase B is only the recurrence and the y accumulation.
 #pragma unroll
-      for (int q = 0; q < SSM_FWD_SUB; ++q) {
-        const int tt = t0s + q;
-        float2 acc = make_float2(yd[q], 0.f);
+      for (int t0s = 0; t0s < TC; t0s += SSM_FWD_SUB) {
+        float2 av[SSM_FWD_SUB][NP], bv[SSM_FWD_SUB][NP], cv[SSM_FWD_SUB][NP];
+        float yd[SSM_FWD_SUB];
 #pragma unroll
-        for (int i = 0; i < NP; ++i) {
-          h[i] = fwd_apply2<METHOD>(h[i], av[q][i], bv[q][i]);
-          if (MODE == kModeMain) acc = fma2(cv[q][i], h[i], acc);
-          else P[i] = mul2(P[i], av[q][i]);
+        for (int q = 0; q < SSM_FWD_SUB; ++q) {
+          const int tt = t0s + q;
+          const float uu = to_f32(Xs[tt * BXC + dl]);
+          const float dtv = to_f32(DLs[tt * BXC + dl]);
+          const float2 u2 = bc2(uu), dt2 = bc2(dtv), dtu2 = bc2(dtv * uu);
+          float2 Bn[NP];
+          loadp<G>(Bs + tt * N + nbase, Bn);
+          if (MODE == kModeMain) loadp<G>(Cs + tt * N + nbase, cv[q]);
+          yd[q] = Dd0 * uu;
+#pragma unroll
+          for (int i = 0; i < NP; ++i)
+            fwd_coeffs2<METHOD>(dt2, u2, dtu2, Bn[i], Ak[i], A2[i], niA[i], av[q][i], bv[q][i]);
+          if (MODE == kModeMain) {   // branch-free: without z the tiles hold zeros
+            const float zz = to_f32(Zs[tt * BXC + dl]);
+            if (g == tt % LPC) zk[tt / LPC] = zz;
+          }
         }
-        yp[(tt % LPC) * YPL + tt / LPC] = acc.x + acc.y;
+#pragma unroll
+        for (int q = 0; q < SSM_FWD_SUB; ++q) {
+          const int tt = t0s + q;
+          float2 acc = make_float2(yd[q], 0.f);
+#pragma unroll
+          for (int i = 0; i < NP; ++i) {
+            h[i] = fwd_apply2<METHOD>(h[i], av[q][i], bv[q][i]);
+            if (MODE == kModeMain) acc = fma2(cv[q][i], h[i], acc);
+            else P[i] = mul2(P[i], av[q][i]);
+          }
+          yp[(tt % LPC) * YPL + tt / LPC] = acc.x + acc.y;
+        }
       }
     }
     // every lane has read this stage: hand it back to the TMA ring
     __syncwarp();
     if (p.use_tma && lane == 0 && ib + S::NSTAGE < nblk)
-      fwd_issue_loads<S, MODE>(p, st, &bars[s], x0, t0 + S::NSTAGE * TC, b);
+      fwd_issue_loads<S, MODE>(p, st, &bars[s], x0, blk_t0(ib + S::NSTAGE), b);
 
     if (MODE == kModeMain) {
       // y over the LPC lanes of the channel: lane g ends with steps g, g + LPC, ...
-      xpose_reduce<TC, LPC, 1>(yp, lane);
+      xpose_reduce<TC, LPC, GSTRIDE>(yp, lane);
 #pragma unroll
       for (int i = 0; i < YPL; ++i) {
         const int t = t0 + g + i * LPC;

@@ -28,11 +28,17 @@ static cudaError_t launch_fwd_n(int method, int mode, const FwdParams& p, dim3 g
       case kEuler: return launch_fwd_nm<T, N, G, kEuler, kModeMain>(p, grid, stream);
       case kBilinear: return launch_fwd_nm<T, N, G, kBilinear, kModeMain>(p, grid, stream);
     }
-  } else {
+  } else if (mode == kModeSummary) {
     switch (method) {
       case kZOH: return launch_fwd_nm<T, N, G, kZOH, kModeSummary>(p, grid, stream);
       case kEuler: return launch_fwd_nm<T, N, G, kEuler, kModeSummary>(p, grid, stream);
       case kBilinear: return launch_fwd_nm<T, N, G, kBilinear, kModeSummary>(p, grid, stream);
+    }
+  } else if (mode == kModeAdjoint) {
+    switch (method) {
+      case kZOH: return launch_fwd_nm<T, N, G, kZOH, kModeAdjoint>(p, grid, stream);
+      case kEuler: return launch_fwd_nm<T, N, G, kEuler, kModeAdjoint>(p, grid, stream);
+      case kBilinear: return launch_fwd_nm<T, N, G, kBilinear, kModeAdjoint>(p, grid, stream);
     }
   }
   return cudaErrorInvalidValue;

@@ -5,6 +5,7 @@ namespace ssm {
 
 // Sequential composition of per-segment summaries, one thread per (b, d, n):
 //   seg_init[s] = carry;  carry = decay[s] * carry + hend[s]       (s = 0 .. S-1)
+// or, for the adjoint summaries (reverse), over s = S-1 .. 0.
 // The chunk-level combine of the reference's two-level scan (models/scan.py:160-164, whose
 // log-depth Hillis-Steele pass over chunk ends is replaced by this O(S) walk per state).
 __global__ void ssm_carry_kernel(const CarryParams p) {
@@ -16,7 +17,8 @@ __global__ void ssm_carry_kernel(const CarryParams p) {
   float dec = 1.0f;
   const size_t base = (size_t)b * p.nseg * dn_total + dn;
 #pragma unroll 4
-  for (int s = 0; s < p.nseg; ++s) {
+  for (int i = 0; i < p.nseg; ++i) {
+    const int s = p.reverse ? p.nseg - 1 - i : i;
     const size_t o = base + (size_t)s * dn_total;
     if (p.seg_init != nullptr) p.seg_init[o] = carry;
     const float a = p.seg_decay[o];

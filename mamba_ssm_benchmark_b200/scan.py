@@ -102,30 +102,38 @@ class SelectiveScanFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy, dlast):
         x, delta, A, Bm, Cm, h0, D, z, cs, yg = ctx.saved_tensors
-        Bsz, L, Dch = x.shape
-        N = A.shape[1]
-        dev = x.device
-        dy = _act(dy, x.dtype)
-        dlast = None if dlast is None else dlast.to(torch.float32).contiguous()
-        du = torch.empty((Bsz, L, Dch), dtype=x.dtype, device=dev)
-        ddelta = torch.empty((Bsz, L, Dch), dtype=x.dtype, device=dev)
-        dA = torch.empty((Dch, N), dtype=torch.float32, device=dev)
-        dB = torch.empty((Bsz, L, N), dtype=x.dtype, device=dev)
-        dC = torch.empty((Bsz, L, N), dtype=x.dtype, device=dev)
-        dD = torch.empty((Dch,), dtype=torch.float32, device=dev) if D is not None else None
-        dz = torch.empty((Bsz, L, Dch), dtype=x.dtype, device=dev) if z is not None else None
-        dh0 = torch.empty((Bsz, Dch, N), dtype=torch.float32, device=dev) if h0 is not None else None
-        wsb = nat.bwd_workspace_bytes(Bsz, L, Dch, N)
-        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
-        with torch.cuda.device(dev):
-            rc = nat.lib().ssm_scan_bwd(
-                Bsz, L, Dch, N, nat.METHODS[ctx.method], nat.view3(x), nat.view3(delta), nat.ptr(A),
-                nat.view3(Bm), nat.view3(Cm), nat.ptr(D), nat.view3(z), nat.ptr(h0), nat.ptr(cs),
-                nat.view3(yg), nat.view3(dy), nat.ptr(dlast), nat.view3(du), nat.view3(ddelta), nat.ptr(dA),
-                nat.view3(dB), nat.view3(dC), nat.ptr(dD), nat.view3(dz), nat.ptr(dh0),
-                ws.data_ptr(), wsb, nat.stream_of(dev))
-        nat.check(rc, "ssm_scan_bwd")
-        return du, ddelta, dA, dB, dC, dh0, dD, dz, None
+        grads = scan_backward(x, delta, A, Bm, Cm, h0, D, z, cs, yg, dy, dlast, ctx.method)
+        return (*grads, None)
+
+
+def scan_backward(x, delta, A, Bm, Cm, h0, D, z, cs, yg, dy, dlast, method):
+    """One ssm_scan_bwd call: returns (du, ddelta, dA, dB, dC, dh0, dD, dz), each None where the
+    input (h0 for dh0) was None.  cs and yg are what the forward saved (chunk_states, the gate
+    input)."""
+    Bsz, L, Dch = x.shape
+    N = A.shape[1]
+    dev = x.device
+    dy = _act(dy, x.dtype)
+    dlast = None if dlast is None else dlast.to(torch.float32).contiguous()
+    du = torch.empty((Bsz, L, Dch), dtype=x.dtype, device=dev)
+    ddelta = torch.empty((Bsz, L, Dch), dtype=x.dtype, device=dev)
+    dA = torch.empty((Dch, N), dtype=torch.float32, device=dev)
+    dB = torch.empty((Bsz, L, N), dtype=x.dtype, device=dev)
+    dC = torch.empty((Bsz, L, N), dtype=x.dtype, device=dev)
+    dD = torch.empty((Dch,), dtype=torch.float32, device=dev) if D is not None else None
+    dz = torch.empty((Bsz, L, Dch), dtype=x.dtype, device=dev) if z is not None else None
+    dh0 = torch.empty((Bsz, Dch, N), dtype=torch.float32, device=dev) if h0 is not None else None
+    wsb = nat.bwd_workspace_bytes(Bsz, L, Dch, N)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = nat.lib().ssm_scan_bwd(
+            Bsz, L, Dch, N, nat.METHODS[method], nat.view3(x), nat.view3(delta), nat.ptr(A),
+            nat.view3(Bm), nat.view3(Cm), nat.ptr(D), nat.view3(z), nat.ptr(h0), nat.ptr(cs),
+            nat.view3(yg), nat.view3(dy), nat.ptr(dlast), nat.view3(du), nat.view3(ddelta), nat.ptr(dA),
+            nat.view3(dB), nat.view3(dC), nat.ptr(dD), nat.view3(dz), nat.ptr(dh0),
+            ws.data_ptr(), wsb, nat.stream_of(dev))
+    nat.check(rc, "ssm_scan_bwd")
+    return du, ddelta, dA, dB, dC, dh0, dD, dz
 
 
 def _prepare(x, delta, A, Bm, Cm, h0, D, z, method):

@@ -17,13 +17,20 @@ carried-in state h_in_r (``compose_prefix``), and finishes its shard from h_in_r
 (``SequenceShard.finish``, ``ssm_scan_fwd_finish``).  This is the reference's two-level chunked scan (models/scan.py:142-165:
 per-chunk scans, a combine over chunk ends, a fix-up) with one chunk per GPU; the all-gather
 replaces a rank-to-rank chain, so no rank waits on its predecessors' finish passes.
+
+The backward of a sequence shard needs the adjoint entering it from the right, which is affine in
+the next shard's: every rank computes its adjoint summary (``ssm_scan_bwd_summary``: the gradient
+w.r.t. its initial state from a zero adjoint at its end, and its decay product), the summaries are
+all-gathered and composed from the last shard to the first (``compose_suffix``), and every rank runs
+the full backward of its shard with its incoming adjoint (the reverse adjoint of
+models/scan.py:239-240, carried across shards).
 """
 
 import torch
 import torch.distributed as dist
 
 from . import _native as nat
-from .scan import _prepare
+from .scan import CHUNK, _act, _prepare, scan_backward
 
 
 # ------------------------------------------------------------------------------------------------
@@ -97,14 +104,17 @@ def compose_prefix(decays, hends, h0=None):
 # sequence shards: the two kernel phases (CUDA)
 # ------------------------------------------------------------------------------------------------
 class SequenceShard:
-    """The two kernel phases over one contiguous shard of a sequence.
+    """The kernel phases over one contiguous shard of a sequence.
 
     ``summary()`` scans the shard from a zero state (``ssm_scan_fwd_summary``) and returns
     (decay, hend), each (B, D, N) float32: the product of the shard's per-step decays and its end
     state from zero.  ``finish(h_in)`` scans it again from the carried-in state
-    (``ssm_scan_fwd_finish``) and returns (y, last) like ``selective_scan_fused`` with h0 = h_in.
-    Both phases share one workspace, through which the kernels pass per-block summaries from the
-    first phase to the second, so they must run in this order on the same stream."""
+    (``ssm_scan_fwd_finish``) and returns (y, last) like ``selective_scan_fused`` with h0 = h_in;
+    with ``save=True`` it also keeps what the backward needs.  Both phases share one workspace,
+    through which the kernels pass per-block summaries from the first phase to the second, so they
+    must run in this order on the same stream.  ``adjoint_summary(dy)`` (``ssm_scan_bwd_summary``)
+    is the backward's first phase: the gradient with respect to the shard's initial state when no
+    adjoint enters from the right, and the decay product."""
 
     def __init__(self, x, delta, A, Bm, Cm, method="zoh", D=None, z=None):
         self.in_dtype = x.dtype
@@ -117,11 +127,15 @@ class SequenceShard:
         self.wsb = nat.fwd_workspace_bytes(*self.shape)
         self.ws = torch.empty(max(self.wsb, 1), dtype=torch.uint8, device=self.dev)
         self._summarised = False
+        self.chunk_states = self.ygate = self.h_in = None
+
+    def _state(self):
+        Bsz, L, Dch, N = self.shape
+        return torch.empty((Bsz, Dch, N), dtype=torch.float32, device=self.dev)
 
     def summary(self):
         Bsz, L, Dch, N = self.shape
-        decay = torch.empty((Bsz, Dch, N), dtype=torch.float32, device=self.dev)
-        hend = torch.empty((Bsz, Dch, N), dtype=torch.float32, device=self.dev)
+        decay, hend = self._state(), self._state()
         with torch.cuda.device(self.dev):
             rc = nat.lib().ssm_scan_fwd_summary(Bsz, L, Dch, N, nat.METHODS[self.method], nat.view3(self.x),
                                                 nat.view3(self.delta), nat.ptr(self.A), nat.view3(self.Bm),
@@ -131,35 +145,119 @@ class SequenceShard:
         self._summarised = True
         return decay, hend
 
-    def finish(self, h_in):
+    def finish(self, h_in, save=False):
         if not self._summarised:
             raise RuntimeError("SequenceShard.finish needs summary() to have run first")
         Bsz, L, Dch, N = self.shape
         h_in = h_in.to(torch.float32).contiguous()
         y = torch.empty((Bsz, L, Dch), dtype=self.x.dtype, device=self.dev)
-        last = torch.empty((Bsz, Dch, N), dtype=torch.float32, device=self.dev)
+        last = self._state()
+        if save:
+            self.h_in = h_in
+            self.chunk_states = torch.empty((Bsz, -(-L // CHUNK), Dch, N), dtype=torch.float32, device=self.dev)
+            self.ygate = torch.empty_like(y) if self.z is not None else None
         with torch.cuda.device(self.dev):
             rc = nat.lib().ssm_scan_fwd_finish(Bsz, L, Dch, N, nat.METHODS[self.method], nat.view3(self.x),
                                                nat.view3(self.delta), nat.ptr(self.A), nat.view3(self.Bm),
                                                nat.view3(self.Cm), nat.ptr(self.D), nat.view3(self.z),
-                                               nat.ptr(h_in), nat.view3(y), nat.NULL_VIEW, nat.ptr(last), None,
+                                               nat.ptr(h_in), nat.view3(y), nat.view3(self.ygate if save else None),
+                                               nat.ptr(last), nat.ptr(self.chunk_states if save else None),
                                                self.ws.data_ptr(), self.wsb, nat.stream_of(self.dev))
         nat.check(rc, "ssm_scan_fwd_finish")
         return y.to(self.in_dtype), last
 
+    def adjoint_summary(self, dy):
+        Bsz, L, Dch, N = self.shape
+        dy = _act(dy, self.x.dtype)
+        decay, dstart = self._state(), self._state()
+        with torch.cuda.device(self.dev):
+            rc = nat.lib().ssm_scan_bwd_summary(Bsz, L, Dch, N, nat.METHODS[self.method], nat.view3(self.delta),
+                                                nat.ptr(self.A), nat.view3(self.Cm), nat.view3(self.z),
+                                                nat.view3(dy), nat.ptr(decay), nat.ptr(dstart), self.ws.data_ptr(),
+                                                self.wsb, nat.stream_of(self.dev))
+        nat.check(rc, "ssm_scan_bwd_summary")
+        return decay, dstart
+
+    def backward(self, dy, dlast):
+        """ssm_scan_bwd over the shard from its saved forward, with ``dlast`` the adjoint entering
+        from the right.  Returns (du, ddelta, dA, dB, dC, dh_in, dD, dz): dh_in is the gradient
+        w.r.t. the shard's carried-in state; dA, dD are this shard's part of the sums over time."""
+        if self.chunk_states is None:
+            raise RuntimeError("SequenceShard.backward needs finish(..., save=True) first")
+        return scan_backward(self.x, self.delta, self.A, self.Bm, self.Cm, self.h_in, self.D, self.z,
+                             self.chunk_states, self.ygate, dy, dlast, self.method)
+
+
+def compose_suffix(decays, dstarts, dlast=None):
+    """Adjoint entering every shard from the right, and the gradient w.r.t. the first shard's
+    initial state (h0 of the whole sequence).
+
+    decays, dstarts: (W, B, D, N) adjoint summaries of shards 0..W-1 in sequence order;
+    dlast: (B, D, N) gradient of the whole sequence's final state, or None.
+    dl_in[W-1] = dlast, dl_in[r] = dstarts[r+1] + decays[r+1] * dl_in[r+1];
+    dh0 = dstarts[0] + decays[0] * dl_in[0]."""
+    W = decays.shape[0]
+    g = torch.zeros_like(dstarts[0]) if dlast is None else dlast.to(torch.float32)
+    dl_in = torch.empty_like(dstarts)
+    for r in range(W - 1, -1, -1):
+        dl_in[r] = g
+        g = torch.addcmul(dstarts[r], decays[r], g)
+    return dl_in, g
+
+
+def _rank(group):
+    return dist.get_rank(group) if dist.is_initialized() else 0
+
+
+def _world(group):
+    return dist.get_world_size(group) if dist.is_initialized() else 1
+
+
+class SequenceShardedScanFn(torch.autograd.Function):
+    """Autograd over the sequence-sharded scan.  Forward: summary, all-gather, prefix, finish.
+    Backward: adjoint summary, all-gather, suffix, full backward of the shard; dA, dD (sums over
+    the whole sequence) are all-reduced, and dh0 comes out of the suffix composition on every rank."""
+
+    @staticmethod
+    def forward(ctx, x, delta, A, Bm, Cm, h0, D, z, method, group):
+        shard = SequenceShard(x, delta, A, Bm, Cm, method, D, z)
+        decay, hend = shard.summary()
+        decays, hends = exchange_summaries(decay, hend, group)
+        h_in, last = compose_prefix(decays, hends, h0)
+        need_bwd = any(ctx.needs_input_grad[:8])
+        y, _ = shard.finish(h_in[_rank(group)], save=need_bwd)
+        ctx.shard, ctx.group, ctx.has_h0 = (shard if need_bwd else None), group, h0 is not None
+        return y, last
+
+    @staticmethod
+    def backward(ctx, dy, dlast):
+        shard, group = ctx.shard, ctx.group
+        world, rank = _world(group), _rank(group)
+        # the whole sequence's final state is replicated: its gradient is the sum of every rank's
+        dl = torch.zeros(shard.shape[0], shard.shape[2], shard.shape[3], dtype=torch.float32, device=shard.dev)
+        if dlast is not None:
+            dl.copy_(dlast)
+        if world > 1:
+            dist.all_reduce(dl, group=group)
+        decay, dstart = shard.adjoint_summary(dy)
+        decays, dstarts = exchange_summaries(decay, dstart, group)
+        dl_in, dh0 = compose_suffix(decays, dstarts, dl)
+        du, ddelta, dA, dB, dC, _, dD, dz = shard.backward(dy, dl_in[rank])
+        reduce_shared_grads([dA, dD], group)        # each rank holds its shard's share of the time sums
+        return du, ddelta, dA, dB, dC, (dh0 if ctx.has_h0 else None), dD, dz, None, None
+
 
 def sequence_sharded_scan(x, delta, A, Bm, Cm, h0=None, method="zoh", D=None, z=None, group=None):
-    """Forward of one sequence split over the ranks of ``group``: this rank holds shard ``rank``
-    (x, delta, z: (B, L_shard, D); Bm, Cm: (B, L_shard, N)); A, D, h0 are replicated.
-    Returns (y_shard, last) where last is the final state of the WHOLE sequence (on every rank)."""
-    shard = SequenceShard(x, delta, A, Bm, Cm, method, D, z)
-    decay, hend = shard.summary()
-    decays, hends = exchange_summaries(decay, hend, group)
-    rank = dist.get_rank(group) if dist.is_initialized() else 0
-    h_in, last = compose_prefix(decays, hends, h0)
-    y, _ = shard.finish(h_in[rank])
-    return y, last
+    """Selective scan of one sequence split over the ranks of ``group`` (differentiable).
+
+    This rank holds shard ``rank``: x, delta, z: (B, L_shard, D); Bm, Cm: (B, L_shard, N); A, D,
+    h0 are replicated.  Returns (y_shard, last) where last is the final state of the WHOLE
+    sequence (on every rank).  Gradients: du, ddelta, dz, dBm, dCm for this shard's rows; dA, dD
+    and dh0 for the whole sequence, identical on every rank."""
+    x2, delta2, A2, Bm2, Cm2, h02, D2, z2 = _prepare(x, delta, A, Bm, Cm, h0, D, z, method)
+    y, last = SequenceShardedScanFn.apply(x2, delta2, A2, Bm2, Cm2, h02, D2, z2, method, group)
+    return y.to(x.dtype), last
 
 
-__all__ = ["shard_range", "reduce_shared_grads", "exchange_summaries", "compose_prefix", "SequenceShard",
-           "sequence_sharded_scan"]
+__all__ = ["shard_range", "reduce_shared_grads", "exchange_summaries", "compose_prefix", "compose_suffix",
+           "SequenceShard", "SequenceShardedScanFn", "sequence_sharded_scan"]

@@ -15,6 +15,8 @@ seeded inputs and the reference's outputs:
   fused_cfg.npz                    config-distribution inputs through selective_scan + the
                                    mixer gate (y + x*D)*silu(z) (models/mamba.py:124)
   decode.npz                       the inline decode step of models/mamba.py:113-118
+  bench_inputs.npz                 benchmarks/bench_scan.py:make_inputs (the scan benchmark's
+                                   inputs) at L = 8, for the benchmark in the reference's format
 """
 
 import argparse
@@ -65,10 +67,16 @@ def scan_case(ref_scan, shape, method, with_h0, dtype, scan, seed):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("SSM_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--only", default=None, help="write only this fixture group (e.g. bench_inputs)")
     args = ap.parse_args(argv)
     sys.dont_write_bytecode = True            # never write into the reference checkout
     sys.path.insert(0, args.ref)
     from models import scan as ref             # the reference's models/scan.py
+
+    if args.only == "bench_inputs" or args.only is None:
+        bench_inputs()
+    if args.only is not None:
+        return
 
     torch.manual_seed(0)
     for si, shape in enumerate(SCAN_SHAPES):
@@ -117,6 +125,13 @@ def main(argv=None):
         res[f"state_{method}"] = h
     _save("decode.npz", **{k: _np(v) for k, v in res.items()})
     print("wrote", len([f for f in os.listdir(HERE) if f.endswith(".npz")]), "fixtures to", HERE)
+
+
+def bench_inputs():
+    """The reference scan benchmark's seeded inputs (benchmarks/bench_scan.py:25-32) at L = 8."""
+    from benchmarks.bench_scan import make_inputs as ref_bench_inputs
+    x, delta, A, Bm, Cm = ref_bench_inputs(8, device="cpu")
+    _save("bench_inputs.npz", x=_np(x), delta=_np(delta), A=_np(A), Bm=_np(Bm), Cm=_np(Cm))
 
 
 if __name__ == "__main__":

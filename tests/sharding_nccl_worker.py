@@ -45,6 +45,24 @@ def main():
         print(f"rank {rank}: sequence shard [{lo},{hi}) y err {e_y:.2e} last err {e_l:.2e}", flush=True)
         ok &= e_y < 1e-5 and e_l < 1e-5
 
+        # sequence shards, backward: shard gradients and the replicated dA, dD, dh0
+        keys = ("u", "delta", "A", "Bm", "Cm", "Dskip", "z", "h0")
+        full = {k: ins[k].clone().requires_grad_() for k in keys}
+        yf, lf = selective_scan_fused(full["u"], full["delta"], full["A"], full["Bm"], full["Cm"], h0=full["h0"],
+                                      D=full["Dskip"], z=full["z"])
+        dy = torch.randn(yf.shape, device=dev, generator=torch.Generator(device=dev).manual_seed(5))
+        gf = dict(zip(keys, torch.autograd.grad(yf, [full[k] for k in keys], dy)))
+        sh = {k: (ins[k][:, lo:hi] if k in ("u", "delta", "Bm", "Cm", "z") else ins[k]).clone().requires_grad_()
+              for k in keys}
+        ys, _ = sharding.sequence_sharded_scan(sh["u"], sh["delta"], sh["A"], sh["Bm"], sh["Cm"], h0=sh["h0"],
+                                               D=sh["Dskip"], z=sh["z"])
+        gs = dict(zip(keys, torch.autograd.grad(ys, [sh[k] for k in keys], dy[:, lo:hi])))
+        for k in keys:
+            want = gf[k][:, lo:hi] if k in ("u", "delta", "Bm", "Cm", "z") else gf[k]
+            e = err(gs[k], want)
+            ok &= e < 1e-4
+            print(f"rank {rank}: sequence shard grad {k} err {e:.2e}", flush=True)
+
         # channel shards
         B, L, D, N = 4, 512, 256, 16
         ins = make_inputs(B, L, D, N, seed=22, dist="config", device=dev)

@@ -7,6 +7,9 @@ between GPUs under NCCL:
 * sequence shards: every rank summarises its contiguous piece of the sequence, the summaries
   are all-gathered, and the composed carried-in state must equal the full-sequence oracle's
   state at the shard boundary (and the shard's output, finished from it, the oracle's output);
+* sequence-shard backward: every rank summarises its shard's reverse adjoint, the summaries are
+  all-gathered and composed from the last shard to the first, and the adjoint entering each
+  shard (and the gradient of h0) must equal the full-sequence oracle's;
 * channel shards: every rank differentiates its channel range; after ``reduce_shared_grads``
   dBm and dCm must equal the full-width oracle's gradients, for separate tensors and for
   dB | dC views of one buffer.
@@ -68,6 +71,47 @@ def _sequence_worker(rank, world, port, method, with_h0):
         dist.destroy_process_group()
 
 
+def _adjoint(a, cdys, dl=None):
+    """Reverse adjoint over dim 1 from dl (zeros if None): dh_{t-1} = a_t (dh_t + C_t dys_t).
+    Returns the adjoint entering every step from the right, index t -> after step t."""
+    L = a.shape[1]
+    dh = torch.zeros_like(a[:, 0]) if dl is None else dl.clone()
+    out = torch.empty_like(a)
+    for t in range(L - 1, -1, -1):
+        out[:, t] = dh
+        dh = a[:, t] * (dh + cdys[:, t])
+    return out, dh
+
+
+def _sequence_bwd_worker(rank, world, port, method):
+    _init(rank, world, port)
+    try:
+        B, L, D, N = 2, 48, 6, 4
+        ins = make_inputs(B, L, D, N, seed=13, dist="test", h0=True, dlast=True)
+        u, delta, A, Bm, Cm, h0, z, dy, dlast = (ins[k] for k in ("u", "delta", "A", "Bm", "Cm", "h0", "z", "dy",
+                                                                 "dlast"))
+        a, _ = O.discretize(delta, A, Bm, u, method)
+        dys = dy * z * torch.sigmoid(z)
+        cdys = Cm[:, :, None, :] * dys[..., None]
+        after, dh_first = _adjoint(a, cdys, dlast)         # full-sequence reverse adjoint
+        bounds = [round(i * L / world) for i in range(world + 1)]
+        lo, hi = bounds[rank], bounds[rank + 1]
+        decay = a[:, lo:hi].prod(1)
+        _, dstart = _adjoint(a[:, lo:hi], cdys[:, lo:hi])
+        decays, dstarts = sharding.exchange_summaries(decay, dstart)
+        dl_in, dh0 = sharding.compose_suffix(decays, dstarts, dlast)
+        assert O.normwise_error(dl_in[rank], after[:, hi - 1]) < 1e-5
+        assert O.normwise_error(dh0, dh_first) < 1e-5
+        # and dh0 is autograd's gradient of the gated output + dlast . last w.r.t. h0
+        lv = {k: ins[k].clone().requires_grad_(k == "h0") for k in ("u", "delta", "A", "Bm", "Cm", "Dskip", "z", "h0")}
+        y, last = O.selective_scan_fused(lv["u"], lv["delta"], lv["A"], lv["Bm"], lv["Cm"], h0=lv["h0"],
+                                         method=method, Dskip=lv["Dskip"], z=lv["z"])
+        (g,) = torch.autograd.grad((y * dy).sum() + (last * dlast).sum(), lv["h0"])
+        assert O.normwise_error(dh0, g) < 1e-5
+    finally:
+        dist.destroy_process_group()
+
+
 def _channel_worker(rank, world, port, one_buffer):
     _init(rank, world, port)
     try:
@@ -106,6 +150,11 @@ def test_sequence_shards_gloo(world, method, with_h0):
     mp.spawn(_sequence_worker, args=(world, _free_port(), method, with_h0), nprocs=world, join=True)
 
 
+@pytest.mark.parametrize("world,method", [(2, "zoh"), (3, "euler")])
+def test_sequence_shards_backward_gloo(world, method):
+    mp.spawn(_sequence_bwd_worker, args=(world, _free_port(), method), nprocs=world, join=True)
+
+
 @pytest.mark.parametrize("one_buffer", [False, True])
 def test_channel_shards_gloo(one_buffer):
     mp.spawn(_channel_worker, args=(2, _free_port(), one_buffer), nprocs=2, join=True)
@@ -121,6 +170,14 @@ def test_shard_range_partitions():
             assert max(sizes) - min(sizes) <= 1
     with pytest.raises(ValueError):
         sharding.shard_range(8, 2, 2)
+
+
+def test_compose_suffix_single_rank():
+    g = torch.Generator().manual_seed(4)
+    dec, dst, dl = (torch.rand(1, 2, 3, 4, generator=g) for _ in range(3))
+    dl_in, dh0 = sharding.compose_suffix(dec, dst, dl[0])
+    assert torch.equal(dl_in[0], dl[0])
+    assert torch.allclose(dh0, dst[0] + dec[0] * dl[0])
 
 
 def test_compose_prefix_single_rank():
