@@ -22,6 +22,10 @@ N > 1  : one process per GPU (torchrun).  Channel sharding, weak scaling: every 
          contiguous shards (strong scaling); each rank summarises its shard, the summaries are
          all-gathered over NCCL and composed, and each rank finishes its shard from its
          carried-in state (mamba_ssm_benchmark_b200/sharding.py).
+--config 4 : the full byte-level Mamba LM (11 blocks, d_model 256) built on these ops
+         (mamba_ssm_benchmark_b200/mixer.py): training step on 16 x 512 Markov bytes including
+         clipping and AdamW (value: tokens/s), and 256-token generation through CUDA-graph
+         decode steps at batch 1 and 64 ("decode": ms/token).
 --impl reference : the reference's CPU scan (the oracle port of models/scan.py, chunked scan +
          recomputing backward) on the host cores, bounded samples of the same workload.
 """
@@ -36,6 +40,7 @@ import sys
 import time
 
 import torch
+import torch.nn.functional as F
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -50,7 +55,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--config", type=int, choices=(1, 2, 3), default=1)
+    ap.add_argument("--config", type=int, choices=(1, 2, 3, 4), default=1)
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -79,6 +84,18 @@ def ncu_traffic(workload):
     except OSError:
         pass
     return None
+
+
+def mufu_bound(cfg, bwd_ms, clk):
+    """The backward's other roofline: special-function (MUFU) throughput.  Every (t, d, n) needs
+    exp(delta A) twice (state recompute and reverse pass) and every (t, d) the gate's sigmoid (ex2 +
+    rcp), at 16 MUFU results per clock per SM (measured on this B200 pool)."""
+    ops = 2 * cfg.B * cfg.L * cfg.D * cfg.N + 2 * cfg.B * cfg.L * cfg.D
+    mhz = clk.get("sm_mhz") or 1965.0
+    peak = 16 * 148 * mhz * 1e6
+    achieved = ops / (bwd_ms / 1e3)
+    return {"ops_per_launch": ops, "unit": "MUFU ops/s", "achieved": achieved, "peak": peak, "frac": achieved / peak,
+            "peak_source": "16 ops/clk/SM (measured ex2 throughput) x 148 SMs x median SM clock"}
 
 
 # --------------------------------------------------------------------------------------------
@@ -450,12 +467,102 @@ def run_sequence_shards(args, cfg, workload, rank, world, device):
         torch.distributed.destroy_process_group()
 
 
+def run_lm(args, rank, world, device):
+    """Config 4: training step and graph decode of the Mamba LM on the sm_100a ops (1 GPU)."""
+    from mamba_ssm_benchmark_b200.mixer import GraphDecoder, MambaLM
+    from mamba_ssm_benchmark_b200.workloads import markov_bytes
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "config": {"workload": "cfg4_mamba_lm"},
+                              "unavailable": "config 4 is a single-GPU workload"}), flush=True)
+        return
+    torch.manual_seed(0)
+    model = MambaLM(n_layers=11, d_model=256, d_state=16, expand=2, d_conv=4).to(device)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+    host = markov_bytes(16, 513, seed=0).pin_memory()
+    data = host.to(device)
+    stream = torch.cuda.current_stream(device)
+
+    def train_step(batch):
+        logits = model(batch[:, :-1])
+        loss = F.cross_entropy(logits.reshape(-1, 256), batch[:, 1:].reshape(-1))
+        loss.backward()
+        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss
+
+    for _ in range(args.warmup):
+        train_step(data)
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        train_step(data)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    tokens = 16 * 512
+    # e2e: the batch comes from pinned host memory and the loss goes back every step
+    loss_host = torch.empty((), dtype=torch.float32, pin_memory=True)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(args.e2e_steps):
+        loss = train_step(host.to(device, non_blocking=True))
+        loss_host.copy_(loss.detach(), non_blocking=True)
+    a1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = a0.elapsed_time(a1) / args.e2e_steps
+
+    decode = {}
+    model.eval()
+    for bsz in (1, 64):
+        with torch.no_grad():
+            prompt = markov_bytes(bsz, 16, seed=bsz).to(device)
+            states = model.init_state(bsz, 16 + 256, device)
+            model(prompt, states, 0)
+            step = GraphDecoder(model, states)
+            tok = prompt[:, -1:]
+            for _ in range(5):
+                step(tok)
+            d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            d0.record(stream)
+            for _ in range(256):
+                tok = step(tok)[:, -1].argmax(-1, keepdim=True)
+            d1.record(stream)
+            torch.cuda.synchronize(device)
+            decode[f"batch{bsz}_ms_per_token"] = d0.elapsed_time(d1) / 256
+            del step, states
+    per_layer = 2 + 4       # conv fwd + scan fwd; scan bwd + finalize + conv bwd + finalize
+    line = {"metric": "Mamba LM training tokens/s (16 x 512, incl. AdamW) and decode ms/token", "value": tokens / ms * 1e3,
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded order-2 Markov bytes)",
+            "config": {"workload": "cfg4_mamba_lm_L11_d256_B16_T512", "layers": 11, "d_model": 256, "d_state": 16,
+                       "global_batch": 16, "seq_len": 512, "optimizer": "AdamW (fused) + clip 1.0"},
+            "decode": decode,
+            "e2e": {"value": tokens / e2e_ms * 1e3, "unit": "tokens/s", "h2d_bytes_per_step": host.numel() * 8,
+                    "d2h_bytes_per_step": 4, "steps": args.e2e_steps},
+            "gpu_launches": args.steps * 11 * per_layer,
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
+                       "samples": clk["samples"]}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     from mamba_ssm_benchmark_b200.workloads import CONFIGS, algorithmic_bytes
-    cfg = CONFIGS[args.config]
-    workload = cfg.name
+    cfg = CONFIGS.get(args.config)
+    workload = cfg.name if cfg is not None else "cfg4_mamba_lm_L11_d256_B16_T512"
     if args.impl == "reference":
+        if cfg is None:
+            if dist_env()[0] == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference arm times the scan path; "
+                                  "config 4 (full LM) has no CPU-reference arm here"}), flush=True)
+            return
         run_reference(args, cfg, workload)
         return
     rank, world, local = dist_env()
@@ -468,25 +575,48 @@ def main():
     if args.config == 2:
         run_sequence_shards(args, cfg, workload, rank, world, device)
         return
+    if args.config == 4:
+        run_lm(args, rank, world, device)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
     from mamba_ssm_benchmark_b200 import sharding
     sets = 4 if args.config == 1 else 1
     steps = [ScanStep(cfg, device, seed=1000 * s + rank, shared_seed=1000 * s) for s in range(sets)]
     stream = torch.cuda.current_stream(device)
     dBC_bufs = [st.dBC for st in steps]
 
+    # N > 1: the dB|dC all-reduce of step i runs on a side stream while step i + 1's forward runs;
+    # a set's next backward (which rewrites its dB|dC buffer) waits for that set's all-reduce.
+    comm = torch.cuda.Stream(device) if world > 1 else None
+    bwd_done = [torch.cuda.Event() for _ in range(sets)]
+    comm_done = [torch.cuda.Event() for _ in range(sets)]
+
     def one(i, ev=None):
-        st = steps[i % sets]
+        k = i % sets
+        st = steps[k]
         st.fwd()
         if ev is not None:
             ev[0].record(stream)
+        if world > 1 and i >= sets:
+            stream.wait_event(comm_done[k])
         st.bwd()
         if ev is not None:
             ev[1].record(stream)
         if world > 1:
-            sharding.reduce_shared_grads([dBC_bufs[i % sets]])
+            bwd_done[k].record(stream)
+            comm.wait_event(bwd_done[k])
+            with torch.cuda.stream(comm):
+                sharding.reduce_shared_grads([dBC_bufs[k]])
+            comm_done[k].record(comm)
+
+    def drain():
+        if comm is not None:
+            stream.wait_stream(comm)
 
     for i in range(args.warmup):
         one(i)
+    drain()
     torch.cuda.synchronize(device)
     K = args.steps
     bev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
@@ -499,6 +629,7 @@ def main():
     e0.record(stream)
     for i in range(K):
         one(i, bev[i])
+    drain()
     e1.record(stream)
     torch.cuda.synchronize(device)
     if world > 1:
@@ -546,7 +677,8 @@ def main():
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6.65 TB/s", "traffic": traffic,
-                         "algorithmic_bytes_per_launch": bwd_bytes, "avg_launch_ms": bwd_ms},
+                         "algorithmic_bytes_per_launch": bwd_bytes, "avg_launch_ms": bwd_ms,
+                         "mufu": mufu_bound(cfg, bwd_ms, clk)},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": args.e2e_steps},
             "gpu_launches": K * steps[0].launches,

@@ -220,6 +220,33 @@ SSM_API int ssm_state_update(int64_t B, int64_t D, int64_t N, int32_t method,
 /* ---------------------------------------------------------------------------------
  * Diagnostics.
  * ------------------------------------------------------------------------------- */
+/* ---------------------------------------------------------------------------------
+ * Causal depthwise conv1d (+ SiLU): the step in front of the scan in the Mamba mixer,
+ * models/mamba.py:100-107 (x transposed to (B, D, L), left-padded with K - 1 zeros or
+ * prefixed with the decode state, nn.Conv1d(D, D, K, groups=D), SiLU, transposed back).
+ * Computed in the (B, L, D) layout directly:
+ *   out[b, t, d] = act(bias[d] + sum_k weight[d, k] x[b, t - (K - 1) + k, d])
+ * with x[b, t < 0, d] = conv_state[b, d, K - 1 + t] (zeros when conv_state is NULL) and
+ * act = SiLU when silu != 0 (identity otherwise).  x, out: (B, L, D) views in fp32 or bf16
+ * (x may be strided, e.g. half of in_proj's output); weight (D, K) and bias (D) fp32;
+ * K in 1..4.  conv_state / new_conv_state: (B, D, K - 1) in x's dtype, optional;
+ * new_conv_state receives the last K - 1 inputs of cat(conv_state, x) (the decode state
+ * update of models/mamba.py:104-105); it may alias conv_state only when the sequence
+ * is one time tile (always for L <= 4, e.g. a decode step; otherwise SSM_ERR_INVALID).
+ * ------------------------------------------------------------------------------- */
+SSM_API int ssm_conv1d_fwd(int64_t B, int64_t L, int64_t D, int64_t K, ssm_view x,
+                   const float* weight, const float* bias, const void* conv_state, int32_t silu,
+                   ssm_view out, void* new_conv_state, void* stream);
+
+/* Backward of ssm_conv1d_fwd without a state (training): dx (B, L, D) in x's dtype,
+ * dweight (D, K) and dbias (D, may be NULL) fp32, summed in a fixed order (deterministic).
+ * Workspace: ssm_conv1d_bwd_workspace_size bytes. */
+SSM_API int ssm_conv1d_bwd_workspace_size(int64_t B, int64_t L, int64_t D, int64_t K, size_t* bytes);
+SSM_API int ssm_conv1d_bwd(int64_t B, int64_t L, int64_t D, int64_t K, ssm_view x,
+                   const float* weight, const float* bias, int32_t silu, ssm_view dout,
+                   ssm_view dx, float* dweight, float* dbias,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
 /* ABI version of the loaded library (SSM_B200_ABI_VERSION). */
 SSM_API int ssm_abi_version(void);
 /* Message for the most recent non-OK status returned on this thread. */

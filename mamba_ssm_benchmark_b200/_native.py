@@ -24,7 +24,7 @@ EXPORTED = (
     "ssm_abi_version", "ssm_last_error_message", "ssm_read_device_error",
     "ssm_scan_fwd_workspace_size", "ssm_scan_fwd", "ssm_scan_bwd_workspace_size", "ssm_scan_bwd",
     "ssm_scan_fwd_summary", "ssm_scan_fwd_finish", "ssm_state_update", "ssm_scan_bwd_noalloc",
-    "ssm_scan_bwd_summary",
+    "ssm_scan_bwd_summary", "ssm_conv1d_fwd", "ssm_conv1d_bwd_workspace_size", "ssm_conv1d_bwd",
 )
 
 
@@ -61,6 +61,9 @@ _SIGNATURES = {
     "ssm_state_update": (ctypes.c_int, [_I64, _I64, _I64, _I32, _P, _V, _V, _P, _V, _V, _P, _V, _V, _P]),
     "ssm_scan_bwd_summary": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _P, _V, _V, _V, _P, _P, _P, _SZ,
                                             _P]),
+    "ssm_conv1d_fwd": (ctypes.c_int, [_I64, _I64, _I64, _I64, _V, _P, _P, _P, _I32, _V, _P, _P]),
+    "ssm_conv1d_bwd_workspace_size": (ctypes.c_int, [_I64, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
+    "ssm_conv1d_bwd": (ctypes.c_int, [_I64, _I64, _I64, _I64, _V, _P, _P, _I32, _V, _V, _P, _P, _P, _SZ, _P]),
     "ssm_scan_bwd_noalloc": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _V, _P, _V, _V, _P, _V, _P,
                                             _P, _V, _V, _P, _V, _V, _P, _V, _V, _P, _V, _P, _P]),
 }
@@ -128,6 +131,12 @@ def ptr(t):
 
 def stream_of(device):
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def conv_workspace_bytes(B, L, D, K):
+    n = _SZ(0)
+    check(lib().ssm_conv1d_bwd_workspace_size(B, L, D, K, ctypes.byref(n)), "ssm_conv1d_bwd_workspace_size")
+    return n.value
 
 
 def fwd_workspace_bytes(B, L, D, N):

@@ -40,6 +40,12 @@
 #ifndef SSM_BWD_HSMEM
 #define SSM_BWD_HSMEM 0
 #endif
+#ifndef SSM_BWD_ACACHE
+// 1: keep the recompute's decays in shared memory for the reverse pass; 0: recompute them on the
+// MUFU (measured faster: config 1 backward 144 us instead of 155 us, the shared-memory pipe being
+// the busier resource)
+#define SSM_BWD_ACACHE 0
+#endif
 
 namespace ssm {
 
@@ -65,7 +71,7 @@ struct BwdSmem {
   // Either the recomputed states (HSMEM) or the decays (ACACHE) are kept in shared memory;
   // the other lives in registers / is recomputed.
   static constexpr bool HSMEM = SSM_BWD_HSMEM != 0 && Gm::NT <= 256;
-  static constexpr bool ACACHE = !HSMEM && Gm::NT <= 256;
+  static constexpr bool ACACHE = SSM_BWD_ACACHE != 0 && !HSMEM && Gm::NT <= 256;
   static constexpr int OFF_AC = OFF_CP + G * TC * N * 4;       // decay cache (TC x NT x G) fp32
   static constexpr int OFF_OUT = OFF_AC + ((ACACHE || HSMEM) ? TC * Gm::NT * G * 4 : 0);   // NOUT x {du, ddelta, dz}
   static constexpr int OFF_RED = OFF_OUT + NOUT * 3 * OUT;     // (TC, NW, 2N) fp32

@@ -77,6 +77,9 @@ __device__ __forceinline__ float2 fwd_apply2(float2 h, float2 a, float2 bco) {
 #ifndef SSM_FWD_SUB
 #define SSM_FWD_SUB 4   // steps per state-independent sub-tile (divides 16)
 #endif
+#ifndef SSM_FWD_PIPE
+#define SSM_FWD_PIPE 1   // reduce and store box i's outputs while box i + 1's steps run
+#endif
 #ifndef SSM_FWD_GMAJOR
 #define SSM_FWD_GMAJOR 1   // lane = g * CPW + c (state group major) instead of c * LPC + g
 #endif
@@ -202,6 +205,30 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
   T* const yout = static_cast<T*>(const_cast<void*>(p.y.ptr)) + b * p.y.sb + d;
   T* const ygout = static_cast<T*>(const_cast<void*>(p.yg.ptr)) + b * p.yg.sb + d;
 
+  // Output of one box: y over the LPC lanes of each channel (lane g ends with steps g, g + LPC,
+  // ...), the gate, and the stores.  tb < 0 marks "no box" (the stores are skipped).
+  auto emit = [&](float (&v)[TC], const float (&zz)[TC / LPC], int tb) {
+    xpose_reduce<TC, LPC, GSTRIDE>(v, lane);
+#pragma unroll
+    for (int i = 0; i < YPL; ++i) {
+      const int t = tb + g + i * LPC;
+      float yv = v[i];
+      if (tb >= 0 && dvalid && t < p.L) {
+        if (p.save_ygate) ygout[(long long)t * p.yg.sl] = from_f32<T>(yv);
+        if (p.has_z) yv *= zz[i] * sigmoid(zz[i]);
+        yout[(long long)t * p.y.sl] = from_f32<T>(yv);
+      }
+    }
+  };
+  // with SSM_FWD_PIPE the previous box's outputs wait here and are emitted from inside the next
+  // box's step loop, so their shuffles, MUFU work and stores overlap the recurrence
+  float ypv[TC], zpv[TC / LPC];
+  int tpv = -1;
+#pragma unroll
+  for (int i = 0; i < TC; ++i) ypv[i] = 0.f;
+#pragma unroll
+  for (int i = 0; i < TC / LPC; ++i) zpv[i] = 0.f;
+
   for (int ib = 0; ib < nblk; ++ib) {
     const int s = ib % S::NSTAGE;
     const int t0 = blk_t0(ib);
@@ -296,6 +323,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
           }
           yp[(tt % LPC) * YPL + tt / LPC] = acc.x + acc.y;
         }
+        if (SSM_FWD_PIPE && MODE == kModeMain && t0s == (TC > SSM_FWD_SUB ? SSM_FWD_SUB : 0)) emit(ypv, zpv, tpv);
       }
     }
     // every lane has read this stage: hand it back to the TMA ring
@@ -304,22 +332,20 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
       fwd_issue_loads<S, MODE>(p, st, &bars[s], x0, blk_t0(ib + S::NSTAGE), b);
 
     if (MODE == kModeMain) {
-      // y over the LPC lanes of the channel: lane g ends with steps g, g + LPC, ...
-      xpose_reduce<TC, LPC, GSTRIDE>(yp, lane);
+      if (SSM_FWD_PIPE) {
 #pragma unroll
-      for (int i = 0; i < YPL; ++i) {
-        const int t = t0 + g + i * LPC;
-        float yv = yp[i];
-        if (dvalid && t < p.L) {
-          if (p.save_ygate) ygout[(long long)t * p.yg.sl] = from_f32<T>(yv);
-          if (p.has_z) yv *= zk[i] * sigmoid(zk[i]);
-          yout[(long long)t * p.y.sl] = from_f32<T>(yv);
-        }
+        for (int i = 0; i < TC; ++i) ypv[i] = yp[i];
+#pragma unroll
+        for (int i = 0; i < YPL; ++i) zpv[i] = zk[i];
+        tpv = t0;
+      } else {
+        emit(yp, zk, t0);
       }
     }
   }
 
   if (MODE == kModeMain) {
+    if (SSM_FWD_PIPE) emit(ypv, zpv, tpv);
     if (dvalid && t_end == p.L && p.last != nullptr) storep<G>(p.last + ((size_t)b * p.D + d) * N + nbase, h);
   } else if (dvalid) {
     const size_t o = (((size_t)b * p.nseg + seg) * p.D + d) * N + nbase;

@@ -87,3 +87,23 @@ def algorithmic_bytes(B, L, D, N, elem_bytes, fused=True, backward=True):
     fwd = (4 if fused else 3) * bld * elem_bytes + 2 * bln * elem_bytes + D * N * 4 + D * 4 + B * D * N * 4
     bwd = (7 if fused else 5) * bld * elem_bytes + 4 * bln * elem_bytes + 2 * D * N * 4 + 2 * D * 4
     return fwd, (bwd if backward else 0)
+
+
+def markov_bytes(batch, length, seed=0, order=2, vocab=256, temperature=0.5):
+    """(batch, length) int64 bytes from a seeded random order-2 Markov chain over 256 symbols: the
+    next-byte distribution for every (previous, current) pair is a softmax of N(0, 1) / temperature
+    logits, i.e. a (256, 256, 256) transition table drawn from ``seed``.  Generated on the CPU, one
+    position at a time for all rows.  (The config-4 training data; the reference has no such
+    generator and trains on enwik8.)"""
+    if order != 2:
+        raise ValueError("only the order-2 chain is defined")
+    g = torch.Generator().manual_seed(seed)
+    table = torch.softmax(torch.randn(vocab, vocab, vocab, generator=g) / temperature, dim=-1)
+    cdf = table.cumsum(-1)
+    out = torch.empty(batch, length, dtype=torch.long)
+    out[:, :2] = torch.randint(0, vocab, (batch, 2), generator=g)
+    for t in range(2, length):
+        u = torch.rand(batch, 1, generator=g)
+        row = cdf[out[:, t - 2], out[:, t - 1]]
+        out[:, t] = torch.searchsorted(row, u).squeeze(1).clamp_(max=vocab - 1)
+    return out

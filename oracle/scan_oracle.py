@@ -244,3 +244,24 @@ def normwise_error(got, ref):
     ref = ref.detach().double().cpu()
     den = ref.abs().max().item()
     return (got - ref).abs().max().item() / (den if den > 0 else 1.0)
+
+
+def causal_conv1d(x, weight, bias=None, silu=True, conv_state=None):
+    """The mixer's causal depthwise conv (models/mamba.py:100-107), (B, L, D) in and out.
+
+    weight (D, K) (nn.Conv1d's (D, 1, K) squeezed), bias (D) or None; conv_state (B, D, K-1)
+    prefixes the inputs when given (decode), else K-1 zeros do.  Returns (out, new_state) with
+    new_state the last K-1 inputs of the padded/prefixed sequence (models/mamba.py:104-105)."""
+    Bsz, L, D = x.shape
+    K = weight.shape[-1]
+    xc = x.transpose(1, 2)
+    if conv_state is None:
+        xc = torch.nn.functional.pad(xc, (K - 1, 0))
+    else:
+        xc = torch.cat([conv_state.to(xc.dtype), xc], dim=-1)
+    new_state = xc[..., xc.shape[-1] - (K - 1):]
+    out = torch.nn.functional.conv1d(xc, weight.reshape(D, 1, K).to(xc.dtype),
+                                     None if bias is None else bias.to(xc.dtype), groups=D)
+    if silu:
+        out = torch.nn.functional.silu(out)
+    return out.transpose(1, 2), new_state

@@ -17,6 +17,9 @@ seeded inputs and the reference's outputs:
   decode.npz                       the inline decode step of models/mamba.py:113-118
   bench_inputs.npz                 benchmarks/bench_scan.py:make_inputs (the scan benchmark's
                                    inputs) at L = 8, for the benchmark in the reference's format
+  lm_small.npz                     models/lm.py:LM with layers "MM", d_model 32: parameters,
+                                   logits, cross-entropy loss and its parameter gradients on a
+                                   byte batch, and prefill + 4 decode steps with states
 """
 
 import argparse
@@ -75,6 +78,8 @@ def main(argv=None):
 
     if args.only == "bench_inputs" or args.only is None:
         bench_inputs()
+    if args.only == "lm_small" or args.only is None:
+        lm_small()
     if args.only is not None:
         return
 
@@ -125,6 +130,28 @@ def main(argv=None):
         res[f"state_{method}"] = h
     _save("decode.npz", **{k: _np(v) for k, v in res.items()})
     print("wrote", len([f for f in os.listdir(HERE) if f.endswith(".npz")]), "fixtures to", HERE)
+
+
+def lm_small():
+    """A two-block Mamba LM of the reference, seeded, in float32 on the CPU."""
+    from models.lm import LM, LMConfig
+    torch.manual_seed(0)
+    model = LM(LMConfig(layers="MM", d_model=32, d_state=16, expand=2, d_conv=4, scan="chunked"))
+    g = torch.Generator().manual_seed(1)
+    idx = torch.randint(0, 256, (2, 24), generator=g)
+    logits = model(idx)
+    loss = torch.nn.functional.cross_entropy(logits.view(-1, 256), idx.view(-1))
+    names = [n for n, _ in model.named_parameters()]
+    grads = torch.autograd.grad(loss, [p for _, p in model.named_parameters()])
+    res = {"idx": idx, "logits": logits, "loss": loss.reshape(1)}
+    res.update({"p." + k: v for k, v in model.state_dict().items()})
+    res.update({"g." + n: gr for n, gr in zip(names, grads)})
+    with torch.no_grad():
+        states = model.init_state(2, 40, "cpu")
+        res["prefill_logits"] = model(idx[:, :16], states, 0)
+        for i in range(4):
+            res[f"step{i}_logits"] = model(idx[:, 16 + i:17 + i], states, 16 + i)
+    _save("lm_small.npz", **{k: _np(v) for k, v in res.items()})
 
 
 def bench_inputs():
