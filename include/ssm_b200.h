@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define SSM_B200_ABI_VERSION 4
+#define SSM_B200_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define SSM_API __attribute__((visibility("default")))
@@ -216,6 +216,61 @@ SSM_API int ssm_state_update(int64_t B, int64_t D, int64_t N, int32_t method,
                      float* state, ssm_view x, ssm_view delta, const float* A,
                      ssm_view Bm, ssm_view Cm, const float* Dskip, ssm_view z,
                      ssm_view y, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Step-size activation inside the scan.  The mixer computes
+ *   delta = softplus(dt_proj(dt)) = softplus(dt @ W^T + bias)       (models/mamba.py:77)
+ * With opts->softplus != 0 the _ex entry points take the raw dt @ W^T as `delta` and
+ * apply softplus(delta + bias) in registers (torch's threshold: x > 20 gives x); the
+ * backward then writes ddelta as the gradient w.r.t. that raw input and, when
+ * opts->dbias is given, d loss / d bias (D) fp32, summed in a fixed order.  bias (D)
+ * fp32 may be NULL (zero).  opts == NULL or softplus == 0: plain ssm_scan_fwd/_bwd.
+ * ------------------------------------------------------------------------------- */
+typedef struct ssm_delta_opts {
+  const float* bias;
+  int32_t softplus;
+  int32_t reserved;
+  float* dbias;
+} ssm_delta_opts;
+
+SSM_API int ssm_scan_fwd_ex(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method,
+                    ssm_view u, ssm_view delta, const float* A, ssm_view Bm, ssm_view Cm,
+                    const float* Dskip, ssm_view z, const float* h0,
+                    ssm_view y, ssm_view ygate, float* last, float* chunk_states,
+                    const ssm_delta_opts* opts,
+                    void* workspace, size_t workspace_bytes, void* stream);
+SSM_API int ssm_scan_bwd_ex(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method,
+                    ssm_view u, ssm_view delta, const float* A, ssm_view Bm, ssm_view Cm,
+                    const float* Dskip, ssm_view z, const float* h0,
+                    const float* chunk_states, ssm_view ygate, ssm_view dy, const float* dlast,
+                    ssm_view du, ssm_view ddelta, float* dA, ssm_view dBm, ssm_view dCm,
+                    float* dDskip, ssm_view dz, float* dh0,
+                    const ssm_delta_opts* opts,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * The three core entry points under the names the reference's Python API uses for
+ * this path (selective_scan_triton's forward/backward, kernels/triton_scan.py:322;
+ * the decode step of models/mamba.py:113-118 as selective_state_update), for FFI
+ * users who bind by those names.  Same signatures and behaviour as ssm_scan_fwd,
+ * ssm_scan_bwd and ssm_state_update.
+ * ------------------------------------------------------------------------------- */
+SSM_API int selective_scan_fwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method,
+                       ssm_view u, ssm_view delta, const float* A, ssm_view Bm, ssm_view Cm,
+                       const float* Dskip, ssm_view z, const float* h0,
+                       ssm_view y, ssm_view ygate, float* last, float* chunk_states,
+                       void* workspace, size_t workspace_bytes, void* stream);
+SSM_API int selective_scan_bwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method,
+                       ssm_view u, ssm_view delta, const float* A, ssm_view Bm, ssm_view Cm,
+                       const float* Dskip, ssm_view z, const float* h0,
+                       const float* chunk_states, ssm_view ygate, ssm_view dy, const float* dlast,
+                       ssm_view du, ssm_view ddelta, float* dA, ssm_view dBm, ssm_view dCm,
+                       float* dDskip, ssm_view dz, float* dh0,
+                       void* workspace, size_t workspace_bytes, void* stream);
+SSM_API int selective_state_update(int64_t B, int64_t D, int64_t N, int32_t method,
+                           float* state, ssm_view x, ssm_view delta, const float* A,
+                           ssm_view Bm, ssm_view Cm, const float* Dskip, ssm_view z,
+                           ssm_view y, void* stream);
 
 /* ---------------------------------------------------------------------------------
  * Diagnostics.

@@ -17,7 +17,7 @@ SSM_OK, SSM_ERR_INVALID, SSM_ERR_DTYPE, SSM_ERR_WORKSPACE, SSM_ERR_CUDA, SSM_ERR
 SSM_F32, SSM_BF16 = 0, 1
 METHODS = {"zoh": 0, "euler": 1, "bilinear": 2}
 DTYPES = {torch.float32: SSM_F32, torch.bfloat16: SSM_BF16}
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 # Every symbol include/ssm_b200.h declares (checked by the tests).
 EXPORTED = (
@@ -25,6 +25,7 @@ EXPORTED = (
     "ssm_scan_fwd_workspace_size", "ssm_scan_fwd", "ssm_scan_bwd_workspace_size", "ssm_scan_bwd",
     "ssm_scan_fwd_summary", "ssm_scan_fwd_finish", "ssm_state_update", "ssm_scan_bwd_noalloc",
     "ssm_scan_bwd_summary", "ssm_conv1d_fwd", "ssm_conv1d_bwd_workspace_size", "ssm_conv1d_bwd",
+    "selective_scan_fwd", "selective_scan_bwd", "selective_state_update", "ssm_scan_fwd_ex", "ssm_scan_bwd_ex",
 )
 
 
@@ -36,6 +37,12 @@ class SsmView(ctypes.Structure):
     """ssm_view: a (B, rows, cols) tensor with unit stride along cols."""
     _fields_ = [("ptr", ctypes.c_void_p), ("dtype", ctypes.c_int32), ("reserved", ctypes.c_int32),
                 ("batch_stride", ctypes.c_int64), ("row_stride", ctypes.c_int64)]
+
+
+class SsmDeltaOpts(ctypes.Structure):
+    """ssm_delta_opts: delta = softplus(delta + bias) inside the scan; dbias out of the backward."""
+    _fields_ = [("bias", ctypes.c_void_p), ("softplus", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("dbias", ctypes.c_void_p)]
 
 
 _V = SsmView
@@ -67,6 +74,16 @@ _SIGNATURES = {
     "ssm_scan_bwd_noalloc": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _V, _P, _V, _V, _P, _V, _P,
                                             _P, _V, _V, _P, _V, _V, _P, _V, _V, _P, _V, _P, _P]),
 }
+
+_OPTS = ctypes.POINTER(SsmDeltaOpts)
+_SIGNATURES["ssm_scan_fwd_ex"] = (ctypes.c_int, _SIGNATURES["ssm_scan_fwd"][1][:17] + [_OPTS] +
+                                  _SIGNATURES["ssm_scan_fwd"][1][17:])
+_SIGNATURES["ssm_scan_bwd_ex"] = (ctypes.c_int, _SIGNATURES["ssm_scan_bwd"][1][:25] + [_OPTS] +
+                                  _SIGNATURES["ssm_scan_bwd"][1][25:])
+# the reference-named aliases share their counterparts' signatures
+_SIGNATURES["selective_scan_fwd"] = _SIGNATURES["ssm_scan_fwd"]
+_SIGNATURES["selective_scan_bwd"] = _SIGNATURES["ssm_scan_bwd"]
+_SIGNATURES["selective_state_update"] = _SIGNATURES["ssm_state_update"]
 
 _lib = None
 _lock = threading.Lock()
@@ -123,6 +140,14 @@ def view2(t):
         return NULL_VIEW
     assert t.dim() == 2 and (t.stride(1) == 1 or t.shape[1] == 1), "inner dimension must be contiguous"
     return SsmView(t.data_ptr(), DTYPES[t.dtype], 0, t.stride(0), 0)
+
+
+def delta_opts(bias, softplus, dbias=None):
+    """ssm_delta_opts for the _ex entry points, or None (plain delta)."""
+    if not softplus:
+        return None
+    return ctypes.byref(SsmDeltaOpts(None if bias is None else bias.data_ptr(), 1, 0,
+                                     None if dbias is None else dbias.data_ptr()))
 
 
 def ptr(t):

@@ -186,7 +186,7 @@ size_t bwd_ws_bytes(int64_t B, int64_t L, int64_t D, int64_t N) {
   const size_t bc = (size_t)B * ndt * L * 2 * N;
   const size_t a = (size_t)B * D * N;
   const size_t dd = (size_t)B * D;
-  return (bc + a + dd) * sizeof(float) + 3 * 256;
+  return (bc + a + 2 * dd) * sizeof(float) + 4 * 256;   // + (B, D) dt_bias partials
 }
 
 float* carve(unsigned char*& cur, size_t nfloat) {
@@ -230,7 +230,7 @@ int check_f32(const char* name, const void* p, bool required) {
 int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm_view u, ssm_view delta,
              const float* A, ssm_view Bm, ssm_view Cm, const float* Dskip, ssm_view z, const float* h0,
              ssm_view y, ssm_view ygate, float* last, float* chunk_states, float* tot_decay, float* tot_hend,
-             void* workspace, size_t workspace_bytes, void* stream_v) {
+             void* workspace, size_t workspace_bytes, void* stream_v, const ssm_delta_opts* opts = nullptr) {
   int rc = check_common(B, L, D, N, method);
   if (rc) return rc;
   if (u.ptr == nullptr) return fail(SSM_ERR_INVALID, "u is required");
@@ -278,6 +278,11 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   p.D = (int)D;
   p.nchunks = (int)((L + kChunk - 1) / kChunk);
   p.has_z = z.ptr != nullptr;
+  if (opts != nullptr && opts->softplus) {
+    if (opts->bias != nullptr && !aligned16(opts->bias)) return fail(SSM_ERR_INVALID, "delta bias must be 16-byte aligned");
+    p.dt_softplus = 1;
+    p.dt_bias = opts->bias;
+  }
 
   // one warp per CTA: its TMA boxes are CPW channels wide, widened to 16 bytes of channels
   const int G = choose_g(B, D, N);
@@ -411,6 +416,29 @@ int ssm_scan_fwd_summary(int64_t B, int64_t L, int64_t D, int64_t N, int32_t met
                   nullptr, decay, hend, workspace, workspace_bytes, stream);
 }
 
+int selective_scan_fwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm_view u, ssm_view delta,
+                       const float* A, ssm_view Bm, ssm_view Cm, const float* Dskip, ssm_view z, const float* h0,
+                       ssm_view y, ssm_view ygate, float* last, float* chunk_states, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  return ssm_scan_fwd(B, L, D, N, method, u, delta, A, Bm, Cm, Dskip, z, h0, y, ygate, last, chunk_states,
+                      workspace, workspace_bytes, stream);
+}
+
+int selective_scan_bwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm_view u, ssm_view delta,
+                       const float* A, ssm_view Bm, ssm_view Cm, const float* Dskip, ssm_view z, const float* h0,
+                       const float* chunk_states, ssm_view ygate, ssm_view dy, const float* dlast, ssm_view du,
+                       ssm_view ddelta, float* dA, ssm_view dBm, ssm_view dCm, float* dDskip, ssm_view dz,
+                       float* dh0, void* workspace, size_t workspace_bytes, void* stream) {
+  return ssm_scan_bwd(B, L, D, N, method, u, delta, A, Bm, Cm, Dskip, z, h0, chunk_states, ygate, dy, dlast, du,
+                      ddelta, dA, dBm, dCm, dDskip, dz, dh0, workspace, workspace_bytes, stream);
+}
+
+int selective_state_update(int64_t B, int64_t D, int64_t N, int32_t method, float* state, ssm_view x,
+                           ssm_view delta, const float* A, ssm_view Bm, ssm_view Cm, const float* Dskip, ssm_view z,
+                           ssm_view y, void* stream) {
+  return ssm_state_update(B, D, N, method, state, x, delta, A, Bm, Cm, Dskip, z, y, stream);
+}
+
 int ssm_scan_bwd_summary(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm_view delta,
                          const float* A, ssm_view Cm, ssm_view z, ssm_view dy, float* decay, float* dstart,
                          void* workspace, size_t workspace_bytes, void* stream) {
@@ -436,6 +464,23 @@ int ssm_scan_bwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm
                  ssm_view ddelta,
                  float* dA, ssm_view dBm, ssm_view dCm, float* dDskip, ssm_view dz, float* dh0, void* workspace,
                  size_t workspace_bytes, void* stream_v) {
+  return ssm_scan_bwd_ex(B, L, D, N, method, u, delta, A, Bm, Cm, Dskip, z, h0, chunk_states, ygate, dy, dlast, du,
+                         ddelta, dA, dBm, dCm, dDskip, dz, dh0, nullptr, workspace, workspace_bytes, stream_v);
+}
+
+int ssm_scan_fwd_ex(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm_view u, ssm_view delta,
+                    const float* A, ssm_view Bm, ssm_view Cm, const float* Dskip, ssm_view z, const float* h0,
+                    ssm_view y, ssm_view ygate, float* last, float* chunk_states, const ssm_delta_opts* opts,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  return fwd_impl(0, B, L, D, N, method, u, delta, A, Bm, Cm, Dskip, z, h0, y, ygate, last, chunk_states, nullptr,
+                  nullptr, workspace, workspace_bytes, stream, opts);
+}
+
+int ssm_scan_bwd_ex(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm_view u, ssm_view delta,
+                    const float* A, ssm_view Bm, ssm_view Cm, const float* Dskip, ssm_view z, const float* h0,
+                    const float* chunk_states, ssm_view ygate, ssm_view dy, const float* dlast, ssm_view du,
+                    ssm_view ddelta, float* dA, ssm_view dBm, ssm_view dCm, float* dDskip, ssm_view dz, float* dh0,
+                    const ssm_delta_opts* opts, void* workspace, size_t workspace_bytes, void* stream_v) {
   int rc = check_common(B, L, D, N, method);
   if (rc) return rc;
   if (u.ptr == nullptr) return fail(SSM_ERR_INVALID, "u is required");
@@ -496,6 +541,12 @@ int ssm_scan_bwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm
   p.part_bc = carve(cur, (size_t)B * ndt * L * 2 * N);
   p.part_A = carve(cur, (size_t)B * D * N);
   p.part_D = carve(cur, (size_t)B * D);
+  p.part_dtb = carve(cur, (size_t)B * D);
+  if (opts != nullptr && opts->softplus) {
+    if (opts->bias != nullptr && !aligned16(opts->bias)) return fail(SSM_ERR_INVALID, "delta bias must be 16-byte aligned");
+    p.dt_softplus = 1;
+    p.dt_bias = opts->bias;
+  }
 
   bool use_tma = tma_ok(u, B, L, D) && tma_ok(delta, B, L, D) && tma_ok(dy, B, L, D) && tma_ok(Bm, B, L, N) &&
                  tma_ok(Cm, B, L, N) && (!has_z || (tma_ok(z, B, L, D) && tma_ok(ygate, B, L, D)));
@@ -524,6 +575,8 @@ int ssm_scan_bwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm
   f.dC = dact(dCm);
   f.dA = dA;
   f.dD = Dskip != nullptr ? dDskip : nullptr;
+  f.part_dtb = p.part_dtb;
+  f.ddt_bias = (p.dt_softplus && opts->dbias != nullptr) ? opts->dbias : nullptr;
   f.B = (int)B;
   f.L = (int)L;
   f.D = (int)D;

@@ -66,7 +66,10 @@ struct BwdSmem {
   static constexpr int OPF = PadPitch<Gm::CPW, float>::value;
   static constexpr int OUT = ((TC * OP * (int)sizeof(T)) + 127) / 128 * 128;
   static constexpr int OFF_DYS = NSTAGE * STAGE;               // dy * silu(z), fp32, padded
-  static constexpr int OFF_BP = OFF_DYS + ((TC * OPF * 4 + 127) / 128) * 128;   // G perms x (16 x N) fp32 B
+  static constexpr int FT = ((TC * OPF * 4 + 127) / 128) * 128;   // one padded (16 x DT) fp32 tile
+  static constexpr int OFF_SDT = OFF_DYS + FT;                 // dt_softplus: delta = softplus(raw + bias)
+  static constexpr int OFF_SSG = OFF_SDT + FT;                 // dt_softplus: sigmoid(raw + bias)
+  static constexpr int OFF_BP = OFF_SSG + FT;                  // G perms x (16 x N) fp32 B
   static constexpr int OFF_CP = OFF_BP + G * TC * N * 4;       // G perms x (16 x N) fp32 C
   // Either the recomputed states (HSMEM) or the decays (ACACHE) are kept in shared memory;
   // the other lives in registers / is recomputed.
@@ -147,6 +150,8 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
   float* __restrict__ SDYS = reinterpret_cast<float*>(smem + S::OFF_DYS);
+  float* __restrict__ SDT = reinterpret_cast<float*>(smem + S::OFF_SDT);
+  float* __restrict__ SSG = reinterpret_cast<float*>(smem + S::OFF_SSG);
   float* __restrict__ SBP = reinterpret_cast<float*>(smem + S::OFF_BP);
   float* __restrict__ SCP = reinterpret_cast<float*>(smem + S::OFF_CP);
   float* __restrict__ SAC = reinterpret_cast<float*>(smem + S::OFF_AC);
@@ -197,6 +202,9 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
 #pragma unroll
   for (int i = 0; i < NP; ++i) dAA[i] = bc2(0.f);
   float dDacc = 0.0f;
+  float dtbacc = 0.0f;         // this thread's share of d loss / d dt_bias for channel dl
+  // the gate pass visits elements e = tid + k NT, always channel d0 + tid % DT
+  const float dtb_gate = (p.dt_softplus && p.dt_bias != nullptr && d0 + tid % DT < p.D) ? p.dt_bias[d0 + tid % DT] : 0.f;
 
   if (p.use_tma) {
     if (tid == 0) {
@@ -258,6 +266,12 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
         }
         SDYS[epf] = dys;
         dDacc = fmaf(dys, uu, dDacc);   // thread tid always sees channel tid % 32
+        if (p.dt_softplus) {            // rows past L keep delta = 0 (identity steps)
+          const float xr = to_f32(DLs[e]) + dtb_gate;
+          const bool in = t0 + e / DT < p.L;
+          SDT[epf] = in ? softplus(xr) : 0.0f;
+          SSG[epf] = in ? sigmoid(xr) : 0.0f;
+        }
       }
       const T* Bs = reinterpret_cast<const T*>(st + S::OFF_B);
       const T* Cs = reinterpret_cast<const T*>(st + S::OFF_C);
@@ -289,7 +303,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
 #pragma unroll
       for (int j = 0; j < TC; ++j) {
         const float uu = to_f32(Xs[j * DT + dl]);
-        const float dtv = to_f32(DLs[j * DT + dl]);
+        const float dtv = p.dt_softplus ? SDT[j * OPF + dl] : to_f32(DLs[j * DT + dl]);
         const float2 u2 = bc2(uu), dt2 = bc2(dtv), dtu2 = bc2(dtv * uu);
         float2 Bn[NP], av[NP];
         loadp<G>(Bp + j * N, Bn);
@@ -328,7 +342,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
       for (int jj = 3; jj >= 0; --jj) {
         const int j = jg * 4 + jj;
         const float uu = to_f32(Xs[j * DT + dl]);
-        const float dtv = to_f32(DLs[j * DT + dl]);
+        const float dtv = p.dt_softplus ? SDT[j * OPF + dl] : to_f32(DLs[j * DT + dl]);
         const float dys = SDYS[j * OPF + dl];
         const float2 u2 = bc2(uu), dt2 = bc2(dtv), dys2 = bc2(dys);
         float2 Bn[NP], Cn[NP], av[NP], hprev[NP];
@@ -457,7 +471,12 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
           const int idx = (g / QDUP) * QPL + v;   // value index: step jg*4 + idx/2, quantity idx%2
           const int j = jg * 4 + (idx >> 1);
           if (idx & 1) {
-            DDTo[j * OP + dl] = from_f32<T>(red[v]);
+            float g = red[v];
+            if (p.dt_softplus) {      // chain rule through softplus(raw + bias)
+              g *= SSG[j * OPF + dl];
+              dtbacc += g;
+            }
+            DDTo[j * OP + dl] = from_f32<T>(g);
           } else {
             DUo[j * OP + dl] = from_f32<T>(fmaf(Dd, SDYS[j * OPF + dl], red[v]));
           }
@@ -506,6 +525,10 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
     for (int w = 0; w < NT / DT; ++w) sdd += SDD[w * DT + tid];
     p.part_D[(size_t)b * p.D + d0 + tid] = sdd;
   }
+  if (p.dt_softplus && p.part_dtb != nullptr) {   // the channel's share sits on its LPC lanes
+    const float t = group_allreduce<LPC, 1>(dtbacc);
+    if (g == 0 && dvalid) p.part_dtb[(size_t)b * p.D + d] = t;
+  }
 }
 
 // Sums the per-CTA dB | dC partials over channel tiles and the dA / dD partials over batch,
@@ -518,7 +541,8 @@ __global__ void ssm_bwd_finalize(const FinParams p) {
   const long long n2 = 2LL * p.N;
   const long long nbc = (long long)p.B * p.L * n2;
   const long long nA = (long long)p.D * p.N;
-  const long long total = nbc + nA + (p.dD != nullptr ? p.D : 0);
+  const long long nDD = p.dD != nullptr ? p.D : 0;
+  const long long total = nbc + nA + nDD + (p.ddt_bias != nullptr ? p.D : 0);
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
        idx += (long long)gridDim.x * blockDim.x) {
     const float* src;
@@ -535,8 +559,12 @@ __global__ void ssm_bwd_finalize(const FinParams p) {
       src = p.part_A + (idx - nbc);
       stride = nA;
       cnt = p.B;
-    } else {
+    } else if (idx < nbc + nA + nDD) {
       src = p.part_D + (idx - nbc - nA);
+      stride = p.D;
+      cnt = p.B;
+    } else {
+      src = p.part_dtb + (idx - nbc - nA - nDD);
       stride = p.D;
       cnt = p.B;
     }
@@ -560,8 +588,10 @@ __global__ void ssm_bwd_finalize(const FinParams p) {
       }
     } else if (idx < nbc + nA) {
       p.dA[idx - nbc] = s;
-    } else {
+    } else if (idx < nbc + nA + nDD) {
       p.dD[idx - nbc - nA] = s;
+    } else {
+      p.ddt_bias[idx - nbc - nA - nDD] = s;
     }
   }
 }

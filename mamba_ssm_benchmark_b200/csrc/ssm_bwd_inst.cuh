@@ -49,7 +49,7 @@ cudaError_t launch_bwd<SSM_ELEM>(int N, int G, int method, const BwdParams& p, d
 
 template <>
 cudaError_t launch_bwd_finalize<SSM_ELEM>(const FinParams& p, cudaStream_t stream) {
-  const long long total = (long long)p.B * p.L * 2 * p.N + (long long)p.D * p.N + p.D;
+  const long long total = (long long)p.B * p.L * 2 * p.N + (long long)p.D * p.N + 2LL * p.D;
   long long blocks = (total + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   ssm_bwd_finalize<SSM_ELEM><<<(unsigned)blocks, 256, 0, stream>>>(p);

@@ -107,6 +107,11 @@ __device__ __forceinline__ void storep(float* p, const float2 (&v)[G / 2]) {
 
 // logistic sigmoid from e^-z = 2^(-z log2 e)
 __device__ __forceinline__ float sigmoid(float z) { return rcp(1.0f + ex2(-z * kLog2e)); }
+// softplus(x) = log(1 + e^x) with torch's default threshold (x > 20 returns x), the step-size
+// activation of models/mamba.py:77: max(x, 0) + log1p(e^-|x|)
+__device__ __forceinline__ float softplus(float x) {
+  return x > 20.0f ? x : fmaxf(x, 0.0f) + log1pf(__expf(-fabsf(x)));
+}
 
 // ------------------------------------------------------------------------------------------
 // Warp transposition-reduce.  v[0..V) hold this lane's partial sums of V quantities; the
@@ -267,9 +272,11 @@ struct alignas(64) FwdParams {
   float* chunk_states;       // (B, nchunks, D, N) or null
   float* seg_hend;           // summary mode: (B, S, D, N)
   float* seg_decay;          // summary mode: (B, S, D, N)
+  const float* dt_bias;      // (D) or null: added to delta before the softplus
   int* err;
   int B, L, D, nchunks, seg_len, nseg;
   int has_z, use_tma, save_ygate;
+  int dt_softplus;           // delta = softplus(delta + dt_bias) in the kernel
 };
 
 struct alignas(64) BwdParams {
@@ -284,9 +291,12 @@ struct alignas(64) BwdParams {
   float* part_bc;            // (B, nDT, L, 2N): per-CTA dB | dC partial sums
   float* part_A;             // (B, D, N)
   float* part_D;             // (B, D)
+  const float* dt_bias;      // (D) or null (see FwdParams)
+  float* part_dtb;           // (B, D): per-batch sums of the raw-delta gradient (dt_softplus)
   int* err;
   int B, L, D, nchunks, ndt;
   int has_z, use_tma;
+  int dt_softplus;           // ddt is then the gradient w.r.t. the raw delta: ddelta * sigmoid(raw + bias)
 };
 
 struct FinParams {
@@ -296,6 +306,8 @@ struct FinParams {
   DAct dB, dC;               // outputs (B, L, N), element type T
   float* dA;                 // (D, N)
   float* dD;                 // (D) or null
+  const float* part_dtb;     // (B, D) or null
+  float* ddt_bias;           // (D) or null
   int B, L, D, N, ndt;
 };
 

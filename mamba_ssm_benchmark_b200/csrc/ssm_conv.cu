@@ -30,6 +30,7 @@ using ssm::from_f32;
 using ssm::to_f32;
 
 constexpr int kThreads = 128;
+constexpr int kU = 4;          // rows loaded per round by each thread
 constexpr int kTTMax = 64;     // time steps per tile, at most (tiles are shortened for small grids)
 
 struct ConvParams {
@@ -123,24 +124,32 @@ __global__ void __launch_bounds__(kThreads) conv_fwd_kernel(const ConvParams p) 
                         : 0.0f;
     }
   }
-  for (int t = t0; t < t1; ++t) {
-    float xv[VEC], o[VEC];
-    load_vec<T, VEC>(xb + (long long)t * p.xsl, xv);
+  // kU rows per round: their loads are issued together, so each thread keeps kU rows in flight
+  for (int tr = t0; tr < t1; tr += kU) {
+    float xr[kU][VEC];
 #pragma unroll
-    for (int v = 0; v < VEC; ++v) {
-      float acc = fmaf(w[K - 1][v], xv[v], bias[v]);
+    for (int u = 0; u < kU; ++u)
+      if (tr + u < t1) load_vec<T, VEC>(xb + (long long)(tr + u) * p.xsl, xr[u]);
 #pragma unroll
-      for (int j = 0; j < K - 1; ++j) acc = fmaf(w[j][v], win[j][v], acc);
-      o[v] = p.silu ? acc * ssm::sigmoid(acc) : acc;
-    }
-    store_vec<T, VEC>(ob + (long long)t * p.osl, o);
+    for (int u = 0; u < kU; ++u) {
+      if (tr + u >= t1) break;
+      float o[VEC];
 #pragma unroll
-    for (int j = 0; j + 1 < K - 1; ++j)
+      for (int v = 0; v < VEC; ++v) {
+        float acc = fmaf(w[K - 1][v], xr[u][v], bias[v]);
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) win[j][v] = win[j + 1][v];
-    if (K > 1) {
+        for (int j = 0; j < K - 1; ++j) acc = fmaf(w[j][v], win[j][v], acc);
+        o[v] = p.silu ? acc * ssm::sigmoid(acc) : acc;
+      }
+      store_vec<T, VEC>(ob + (long long)(tr + u) * p.osl, o);
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) win[K > 1 ? K - 2 : 0][v] = xv[v];
+      for (int j = 0; j + 1 < K - 1; ++j)
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) win[j][v] = win[j + 1][v];
+      if (K > 1) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) win[K > 1 ? K - 2 : 0][v] = xr[u][v];
+      }
     }
   }
   // the last tile leaves the last K - 1 inputs of cat(state, x) as the new decode state
@@ -189,62 +198,76 @@ __global__ void __launch_bounds__(kThreads) conv_bwd_kernel(const ConvParams p) 
   }
   // rows t0 .. t1 + K - 2: g of every row; dx of row t - (K - 1) once its look-ahead is complete
   const int tend = t1 + K - 1;
-  for (int t = t0; t < tend; ++t) {
-    const bool valid = t < p.L;
-    float xv[VEC], gv[VEC];
-    if (valid) {
-      load_vec<T, VEC>(xb + (long long)t * p.xsl, xv);
-      float dv[VEC];
-      load_vec<T, VEC>(gb + (long long)t * p.gsl, dv);
+  for (int tr = t0; tr < tend; tr += kU) {
+    // kU rows per round: their loads are issued together (rows past L read nothing)
+    float xr[kU][VEC], dr[kU][VEC];
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        float pre = fmaf(w[K - 1][v], xv[v], bias[v]);
+    for (int u = 0; u < kU; ++u) {
+      if (tr + u < tend && tr + u < p.L) {
+        load_vec<T, VEC>(xb + (long long)(tr + u) * p.xsl, xr[u]);
+        load_vec<T, VEC>(gb + (long long)(tr + u) * p.gsl, dr[u]);
+      }
+    }
 #pragma unroll
-        for (int j = 0; j < K - 1; ++j) pre = fmaf(w[j][v], xw[j][v], pre);
-        if (p.silu) {
-          const float s = ssm::sigmoid(pre);
-          gv[v] = dv[v] * s * fmaf(pre, 1.0f - s, 1.0f);
-        } else {
-          gv[v] = dv[v];
+    for (int u = 0; u < kU; ++u) {
+      const int t = tr + u;
+      if (t >= tend) break;
+      const bool valid = t < p.L;
+      float xv[VEC], gv[VEC];
+      if (valid) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) xv[v] = xr[u][v];
+        const float (&dv)[VEC] = dr[u];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          float pre = fmaf(w[K - 1][v], xv[v], bias[v]);
+#pragma unroll
+          for (int j = 0; j < K - 1; ++j) pre = fmaf(w[j][v], xw[j][v], pre);
+          if (p.silu) {
+            const float s = ssm::sigmoid(pre);
+            gv[v] = dv[v] * s * fmaf(pre, 1.0f - s, 1.0f);
+          } else {
+            gv[v] = dv[v];
+          }
+        }
+      } else {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) xv[v] = gv[v] = 0.0f;
+      }
+      if (t < t1) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          dbs[v] += gv[v];
+#pragma unroll
+          for (int j = 0; j < K - 1; ++j) dw[j][v] = fmaf(gv[v], xw[j][v], dw[j][v]);
+          dw[K - 1][v] = fmaf(gv[v], xv[v], dw[K - 1][v]);
         }
       }
-    } else {
+      const int s = t - (K - 1);
+      if (s >= t0 && s < t1) {       // dx[s] = sum_k w[k] g[s + K - 1 - k]; g[t] is the newest
+        float o[VEC];
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) xv[v] = gv[v] = 0.0f;
-    }
-    if (t < t1) {
+        for (int v = 0; v < VEC; ++v) {
+          float acc = w[0][v] * gv[v];
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        dbs[v] += gv[v];
-#pragma unroll
-        for (int j = 0; j < K - 1; ++j) dw[j][v] = fmaf(gv[v], xw[j][v], dw[j][v]);
-        dw[K - 1][v] = fmaf(gv[v], xv[v], dw[K - 1][v]);
+          for (int k = 1; k < K; ++k) acc = fmaf(w[k][v], gq[K - 1 - k][v], acc);
+          o[v] = acc;
+        }
+        store_vec<T, VEC>(dxb + (long long)s * p.osl, o);
       }
-    }
-    const int s = t - (K - 1);
-    if (s >= t0 && s < t1) {       // dx[s] = sum_k w[k] g[s + K - 1 - k]; g[t] is the newest
-      float o[VEC];
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        float acc = w[0][v] * gv[v];
+      for (int j = 0; j + 1 < K - 1; ++j)
 #pragma unroll
-        for (int k = 1; k < K; ++k) acc = fmaf(w[k][v], gq[K - 1 - k][v], acc);
-        o[v] = acc;
-      }
-      store_vec<T, VEC>(dxb + (long long)s * p.osl, o);
-    }
+        for (int v = 0; v < VEC; ++v) {
+          xw[j][v] = xw[j + 1][v];
+          gq[j][v] = gq[j + 1][v];
+        }
+      if (K > 1) {
 #pragma unroll
-    for (int j = 0; j + 1 < K - 1; ++j)
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        xw[j][v] = xw[j + 1][v];
-        gq[j][v] = gq[j + 1][v];
-      }
-    if (K > 1) {
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        xw[K > 1 ? K - 2 : 0][v] = xv[v];
-        gq[K > 1 ? K - 2 : 0][v] = gv[v];
+        for (int v = 0; v < VEC; ++v) {
+          xw[K > 1 ? K - 2 : 0][v] = xv[v];
+          gq[K > 1 ? K - 2 : 0][v] = gv[v];
+        }
       }
     }
   }

@@ -171,6 +171,8 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
       niA[i] = make_float2(-1.0f / av[2 * i], -1.0f / av[2 * i + 1]);
     }
   }
+  // step-size bias of the in-kernel softplus (dt_softplus); the zero rows past L keep delta = 0
+  const float dtb = (p.dt_softplus && p.dt_bias != nullptr && dvalid) ? p.dt_bias[d] : 0.0f;
   // D skip folded into the partial sum of lane g == 0 of each channel group
   const float Dd0 = (MODE == kModeMain && p.Dskip != nullptr && dvalid && g == 0) ? p.Dskip[d] : 0.0f;
 
@@ -259,7 +261,8 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
         for (int q = 0; q < SSM_FWD_SUB; ++q) {
           const int tt = t0s + q;
           float dys = to_f32(Xs[tt * BXC + dl]);
-          const float dtv = to_f32(DLs[tt * BXC + dl]);
+          float dtv = to_f32(DLs[tt * BXC + dl]);
+          if (p.dt_softplus) dtv = (t0 + tt < p.L) ? softplus(dtv + dtb) : 0.0f;   // rows past L stay identity steps
           if (p.has_z) {
             const float zz = to_f32(Zs[tt * BXC + dl]);
             dys *= zz * sigmoid(zz);
@@ -297,7 +300,8 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
         for (int q = 0; q < SSM_FWD_SUB; ++q) {
           const int tt = t0s + q;
           const float uu = to_f32(Xs[tt * BXC + dl]);
-          const float dtv = to_f32(DLs[tt * BXC + dl]);
+          float dtv = to_f32(DLs[tt * BXC + dl]);
+          if (p.dt_softplus) dtv = (t0 + tt < p.L) ? softplus(dtv + dtb) : 0.0f;   // rows past L stay identity steps
           const float2 u2 = bc2(uu), dt2 = bc2(dtv), dtu2 = bc2(dtv * uu);
           float2 Bn[NP];
           loadp<G>(Bs + tt * N + nbase, Bn);

@@ -5,7 +5,8 @@ names, shapes and initialisation (so state dicts load either way), the same forw
 (``out = mixer(u, state=None, pos=0)``) and the same decode state.  What changes is the path
 around the scan: the causal conv + SiLU is ``causal_conv1d`` (reads the x half of in_proj's
 output in place), the scan with the D skip and the SiLU(z) gate is one ``selective_scan_fused``
-call, and a decode step (L = 1 with a state) is ``causal_conv1d`` on the conv state plus
+call that also applies the step size's softplus(dt_proj(dt)) (the projection goes in without its
+bias), and a decode step (L = 1 with a state) is ``causal_conv1d`` on the conv state plus
 ``selective_state_update``, both updating the state in place.  The projections stay torch GEMMs.
 
 ``MambaLM`` is models/lm.py:LM restricted to Mamba blocks ("M" * n_layers): embedding, pre-norm
@@ -106,15 +107,26 @@ class MambaMixer(nn.Module):
         else:
             x = causal_conv1d(x.to(state.conv.dtype), self.conv.weight, self.conv.bias, conv_state=state.conv,
                               update_state=True)
-        delta, A, Bm, Cm = self.ssm_params(x)
+        h0 = None if state is None else state.ssm
         if L == 1 and state is not None:                                  # recurrent decode step
+            delta, A, Bm, Cm = self.ssm_params(x)
             y = selective_state_update(state.ssm, x[:, 0], delta[:, 0], A, Bm[:, 0], Cm[:, 0], D=self.D,
                                        method=self.discretization, z=z[:, 0]).unsqueeze(1)
+        elif self.selective:
+            # softplus(dt_proj(dt)) happens inside the scan: the projection without its bias goes in
+            dt, Bm, Cm = self.x_proj(x).split([self.dt_rank, self.d_state, self.d_state], dim=-1)
+            dt_raw = F.linear(dt, self.dt_proj.weight)
+            A = -torch.exp(self.A_log.to(torch.promote_types(x.dtype, torch.float32)))
+            if self.a_mode == "scalar":
+                A = A.expand(-1, self.d_state)
+            y, last = selective_scan_fused(x, dt_raw, A, Bm, Cm, h0=h0, method=self.discretization, D=self.D, z=z,
+                                           delta_bias=self.dt_proj.bias, delta_softplus=True)
+            delta = F.softplus(dt_raw.float() + self.dt_proj.bias) if return_delta else None
         else:
-            h0 = None if state is None else state.ssm
+            delta, A, Bm, Cm = self.ssm_params(x)
             y, last = selective_scan_fused(x, delta, A, Bm, Cm, h0=h0, method=self.discretization, D=self.D, z=z)
-            if state is not None:
-                state.ssm.copy_(last)
+        if state is not None and not (L == 1):
+            state.ssm.copy_(last)
         out = self.out_proj(y)
         return (out, delta) if return_delta else out
 

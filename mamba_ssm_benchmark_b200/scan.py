@@ -75,7 +75,7 @@ class SelectiveScanFn(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, x, delta, A, Bm, Cm, h0, D, z, method):
+    def forward(ctx, x, delta, A, Bm, Cm, h0, D, z, method, delta_bias=None, delta_softplus=False):
         Bsz, L, Dch = x.shape
         N = A.shape[1]
         dev = x.device
@@ -89,27 +89,31 @@ class SelectiveScanFn(torch.autograd.Function):
         wsb = nat.fwd_workspace_bytes(Bsz, L, Dch, N)
         ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
         with torch.cuda.device(dev):
-            rc = nat.lib().ssm_scan_fwd(
+            rc = nat.lib().ssm_scan_fwd_ex(
                 Bsz, L, Dch, N, nat.METHODS[method], nat.view3(x), nat.view3(delta), nat.ptr(A),
                 nat.view3(Bm), nat.view3(Cm), nat.ptr(D), nat.view3(z), nat.ptr(h0),
-                nat.view3(y), nat.view3(yg), nat.ptr(last), nat.ptr(cs), ws.data_ptr(), wsb, nat.stream_of(dev))
+                nat.view3(y), nat.view3(yg), nat.ptr(last), nat.ptr(cs), nat.delta_opts(delta_bias, delta_softplus),
+                ws.data_ptr(), wsb, nat.stream_of(dev))
         nat.check(rc, "ssm_scan_fwd")
         if need_bwd:
-            ctx.save_for_backward(x, delta, A, Bm, Cm, h0, D, z, cs, yg)
+            ctx.save_for_backward(x, delta, A, Bm, Cm, h0, D, z, cs, yg, delta_bias)
         ctx.method = method
+        ctx.delta_softplus = delta_softplus
         return y, last
 
     @staticmethod
     def backward(ctx, dy, dlast):
-        x, delta, A, Bm, Cm, h0, D, z, cs, yg = ctx.saved_tensors
-        grads = scan_backward(x, delta, A, Bm, Cm, h0, D, z, cs, yg, dy, dlast, ctx.method)
-        return (*grads, None)
+        x, delta, A, Bm, Cm, h0, D, z, cs, yg, delta_bias = ctx.saved_tensors
+        grads = scan_backward(x, delta, A, Bm, Cm, h0, D, z, cs, yg, dy, dlast, ctx.method, delta_bias,
+                              ctx.delta_softplus)
+        return (*grads[:8], None, grads[8], None)
 
 
-def scan_backward(x, delta, A, Bm, Cm, h0, D, z, cs, yg, dy, dlast, method):
-    """One ssm_scan_bwd call: returns (du, ddelta, dA, dB, dC, dh0, dD, dz), each None where the
-    input (h0 for dh0) was None.  cs and yg are what the forward saved (chunk_states, the gate
-    input)."""
+def scan_backward(x, delta, A, Bm, Cm, h0, D, z, cs, yg, dy, dlast, method, delta_bias=None, delta_softplus=False):
+    """One ssm_scan_bwd call: returns (du, ddelta, dA, dB, dC, dh0, dD, dz, ddelta_bias), each None
+    where the input (h0 for dh0, delta_bias) was None.  cs and yg are what the forward saved
+    (chunk_states, the gate input).  With delta_softplus, ddelta is the gradient w.r.t. the raw
+    delta (before bias and softplus)."""
     Bsz, L, Dch = x.shape
     N = A.shape[1]
     dev = x.device
@@ -123,17 +127,18 @@ def scan_backward(x, delta, A, Bm, Cm, h0, D, z, cs, yg, dy, dlast, method):
     dD = torch.empty((Dch,), dtype=torch.float32, device=dev) if D is not None else None
     dz = torch.empty((Bsz, L, Dch), dtype=x.dtype, device=dev) if z is not None else None
     dh0 = torch.empty((Bsz, Dch, N), dtype=torch.float32, device=dev) if h0 is not None else None
+    dbias = torch.empty((Dch,), dtype=torch.float32, device=dev) if (delta_softplus and delta_bias is not None) else None
     wsb = nat.bwd_workspace_bytes(Bsz, L, Dch, N)
     ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
-        rc = nat.lib().ssm_scan_bwd(
+        rc = nat.lib().ssm_scan_bwd_ex(
             Bsz, L, Dch, N, nat.METHODS[method], nat.view3(x), nat.view3(delta), nat.ptr(A),
             nat.view3(Bm), nat.view3(Cm), nat.ptr(D), nat.view3(z), nat.ptr(h0), nat.ptr(cs),
             nat.view3(yg), nat.view3(dy), nat.ptr(dlast), nat.view3(du), nat.view3(ddelta), nat.ptr(dA),
             nat.view3(dB), nat.view3(dC), nat.ptr(dD), nat.view3(dz), nat.ptr(dh0),
-            ws.data_ptr(), wsb, nat.stream_of(dev))
+            nat.delta_opts(delta_bias, delta_softplus, dbias), ws.data_ptr(), wsb, nat.stream_of(dev))
     nat.check(rc, "ssm_scan_bwd")
-    return du, ddelta, dA, dB, dC, dh0, dD, dz
+    return du, ddelta, dA, dB, dC, dh0, dD, dz, dbias
 
 
 def _prepare(x, delta, A, Bm, Cm, h0, D, z, method):
@@ -146,15 +151,20 @@ def _prepare(x, delta, A, Bm, Cm, h0, D, z, method):
     return (_act(x, ct), _act(delta, ct), _f32(A), _act(Bm, ct), _act(Cm, ct), _f32(h0), _f32(D), _act(z, ct))
 
 
-def selective_scan_fused(x, delta, A, Bm, Cm, h0=None, method="zoh", D=None, z=None):
+def selective_scan_fused(x, delta, A, Bm, Cm, h0=None, method="zoh", D=None, z=None, delta_bias=None,
+                         delta_softplus=False):
     """Returns (out, last) with out = (scan(x) + x*D) * silu(z) (each term optional).
 
     x, delta, z: (B, L, D); A: (D, N); Bm, Cm: (B, L, N); h0: (B, D, N); D: (D).
+    With ``delta_softplus`` the scan uses softplus(delta + delta_bias) as its step size, computed in
+    the kernels (the mixer's ``F.softplus(dt_proj(dt))``, models/mamba.py:77, with ``delta`` the
+    projection without its bias); gradients flow to the raw delta and to delta_bias (D).
     out has x's dtype; last is float32.
     """
     in_dtype = x.dtype
     args = _prepare(x, delta, A, Bm, Cm, h0, D, z, method)
-    y, last = SelectiveScanFn.apply(*args, method)
+    bias = _f32(delta_bias) if delta_softplus else None
+    y, last = SelectiveScanFn.apply(*args, method, bias, bool(delta_softplus))
     return y.to(in_dtype), last
 
 

@@ -185,7 +185,7 @@ class SequenceShard:
         if self.chunk_states is None:
             raise RuntimeError("SequenceShard.backward needs finish(..., save=True) first")
         return scan_backward(self.x, self.delta, self.A, self.Bm, self.Cm, self.h_in, self.D, self.z,
-                             self.chunk_states, self.ygate, dy, dlast, self.method)
+                             self.chunk_states, self.ygate, dy, dlast, self.method)[:8]
 
 
 def compose_suffix(decays, dstarts, dlast=None):

@@ -16,7 +16,7 @@ HEADER = os.path.join(ROOT, "include", "ssm_b200.h")
 
 def declared_symbols():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"SSM_API\s+[\w\s\*]+?\b(ssm_\w+)\s*\(", text)))
+    return sorted(set(re.findall(r"SSM_API\s+[\w\s\*]+?\b((?:ssm|selective)_\w+)\s*\(", text)))
 
 
 def test_header_declares_every_binding():
