@@ -43,7 +43,8 @@ struct FwdSmem {
   static constexpr int OFF_U = 0, OFF_DT = ACT, OFF_Z = 2 * ACT, OFF_B = 3 * ACT, OFF_C = 3 * ACT + BC;
   static constexpr int STAGE = 3 * ACT + 2 * BC;
   static constexpr int OFF_BAR = NSTAGE * STAGE;
-  static constexpr int BYTES = OFF_BAR + NSTAGE * 8;
+  static constexpr int OFF_SDT = OFF_BAR + NSTAGE * 8;   // dt_softplus: the box's activated deltas (fp32)
+  static constexpr int BYTES = OFF_SDT + TC * BXC * 4;
   static_assert(ACT % 128 == 0 && BC % 128 == 0, "TMA boxes must stay 128-byte aligned");
 };
 
@@ -171,8 +172,6 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
       niA[i] = make_float2(-1.0f / av[2 * i], -1.0f / av[2 * i + 1]);
     }
   }
-  // step-size bias of the in-kernel softplus (dt_softplus); the zero rows past L keep delta = 0
-  const float dtb = (p.dt_softplus && p.dt_bias != nullptr && dvalid) ? p.dt_bias[d] : 0.0f;
   // D skip folded into the partial sum of lane g == 0 of each channel group
   const float Dd0 = (MODE == kModeMain && p.Dskip != nullptr && dvalid && g == 0) ? p.Dskip[d] : 0.0f;
 
@@ -251,6 +250,20 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
     if (MODE == kModeMain && p.chunk_states != nullptr && dvalid)   // state entering chunk t0 / 16
       storep<G>(p.chunk_states + (((size_t)b * p.nchunks + t0 / TC) * p.D + d) * N + nbase, h);
 
+    // dt_softplus: the box's deltas are activated once per element, softplus(raw + bias), into an
+    // fp32 tile (rows past L and columns past D stay 0: identity steps).  The previous box's
+    // readers are done: every lane passed the __syncwarp before that box's refill.
+    float* const SDT = reinterpret_cast<float*>(smem + S::OFF_SDT);
+    if (p.dt_softplus) {
+      for (int e = lane; e < TC * BXC; e += 32) {
+        const int t = t0 + e / BXC, dg = x0 + e % BXC;
+        SDT[e] = (t < p.L && dg < p.D)
+                     ? softplus(to_f32(DLs[e]) + (p.dt_bias != nullptr ? p.dt_bias[dg] : 0.0f))
+                     : 0.0f;
+      }
+      __syncwarp();
+    }
+
     float yp[TC], zk[YPL];   // main mode: partial y and the gate's z (see below)
     if constexpr (MODE == kModeAdjoint) {
       // reverse through the box: dh <- a_t dh + a_t C_t dys_t, dys = dy silu(z) (or dy)
@@ -262,7 +275,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
           const int tt = t0s + q;
           float dys = to_f32(Xs[tt * BXC + dl]);
           float dtv = to_f32(DLs[tt * BXC + dl]);
-          if (p.dt_softplus) dtv = (t0 + tt < p.L) ? softplus(dtv + dtb) : 0.0f;   // rows past L stay identity steps
+          if (p.dt_softplus) dtv = SDT[tt * BXC + dl];
           if (p.has_z) {
             const float zz = to_f32(Zs[tt * BXC + dl]);
             dys *= zz * sigmoid(zz);
@@ -301,7 +314,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
           const int tt = t0s + q;
           const float uu = to_f32(Xs[tt * BXC + dl]);
           float dtv = to_f32(DLs[tt * BXC + dl]);
-          if (p.dt_softplus) dtv = (t0 + tt < p.L) ? softplus(dtv + dtb) : 0.0f;   // rows past L stay identity steps
+          if (p.dt_softplus) dtv = SDT[tt * BXC + dl];
           const float2 u2 = bc2(uu), dt2 = bc2(dtv), dtu2 = bc2(dtv * uu);
           float2 Bn[NP];
           loadp<G>(Bs + tt * N + nbase, Bn);
