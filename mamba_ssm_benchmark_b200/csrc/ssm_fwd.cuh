@@ -81,6 +81,9 @@ __device__ __forceinline__ float2 fwd_apply2(float2 h, float2 a, float2 bco) {
 #ifndef SSM_FWD_PIPE
 #define SSM_FWD_PIPE 1   // reduce and store box i's outputs while box i + 1's steps run
 #endif
+#ifndef SSM_FWD_LATEZ
+#define SSM_FWD_LATEZ 1   // z and the D-skip input are read for the lane's output steps only, at the box end
+#endif
 #ifndef SSM_FWD_GMAJOR
 #define SSM_FWD_GMAJOR 1   // lane = g * CPW + c (state group major) instead of c * LPC + g
 #endif
@@ -173,7 +176,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
     }
   }
   // D skip folded into the partial sum of lane g == 0 of each channel group
-  const float Dd0 = (MODE == kModeMain && p.Dskip != nullptr && dvalid && g == 0) ? p.Dskip[d] : 0.0f;
+  const float Dd0 = (MODE == kModeMain && p.Dskip != nullptr && dvalid && (SSM_FWD_LATEZ || g == 0)) ? p.Dskip[d] : 0.0f;
 
   float2 h[NP], P[NP];
 #pragma unroll
@@ -208,12 +211,12 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
 
   // Output of one box: y over the LPC lanes of each channel (lane g ends with steps g, g + LPC,
   // ...), the gate, and the stores.  tb < 0 marks "no box" (the stores are skipped).
-  auto emit = [&](float (&v)[TC], const float (&zz)[TC / LPC], int tb) {
+  auto emit = [&](float (&v)[TC], const float (&zz)[TC / LPC], const float (&uu)[TC / LPC], int tb) {
     xpose_reduce<TC, LPC, GSTRIDE>(v, lane);
 #pragma unroll
     for (int i = 0; i < YPL; ++i) {
       const int t = tb + g + i * LPC;
-      float yv = v[i];
+      float yv = SSM_FWD_LATEZ ? fmaf(Dd0, uu[i], v[i]) : v[i];
       if (tb >= 0 && dvalid && t < p.L) {
         if (p.save_ygate) ygout[(long long)t * p.yg.sl] = from_f32<T>(yv);
         if (p.has_z) yv *= zz[i] * sigmoid(zz[i]);
@@ -223,12 +226,12 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
   };
   // with SSM_FWD_PIPE the previous box's outputs wait here and are emitted from inside the next
   // box's step loop, so their shuffles, MUFU work and stores overlap the recurrence
-  float ypv[TC], zpv[TC / LPC];
+  float ypv[TC], zpv[TC / LPC], upv[TC / LPC];
   int tpv = -1;
 #pragma unroll
   for (int i = 0; i < TC; ++i) ypv[i] = 0.f;
 #pragma unroll
-  for (int i = 0; i < TC / LPC; ++i) zpv[i] = 0.f;
+  for (int i = 0; i < TC / LPC; ++i) zpv[i] = upv[i] = 0.f;
 
   for (int ib = 0; ib < nblk; ++ib) {
     const int s = ib % S::NSTAGE;
@@ -264,7 +267,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
       __syncwarp();
     }
 
-    float yp[TC], zk[YPL];   // main mode: partial y and the gate's z (see below)
+    float yp[TC], zk[YPL], uk[YPL];   // main mode: partial y; the gate's z and the D-skip u of the lane's output steps
     if constexpr (MODE == kModeAdjoint) {
       // reverse through the box: dh <- a_t dh + a_t C_t dys_t, dys = dy silu(z) (or dy)
 #pragma unroll
@@ -319,11 +322,11 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
           float2 Bn[NP];
           loadp<G>(Bs + tt * N + nbase, Bn);
           if (MODE == kModeMain) loadp<G>(Cs + tt * N + nbase, cv[q]);
-          yd[q] = Dd0 * uu;
+          yd[q] = SSM_FWD_LATEZ ? 0.0f : Dd0 * uu;
 #pragma unroll
           for (int i = 0; i < NP; ++i)
             fwd_coeffs2<METHOD>(dt2, u2, dtu2, Bn[i], Ak[i], A2[i], niA[i], av[q][i], bv[q][i]);
-          if (MODE == kModeMain) {   // branch-free: without z the tiles hold zeros
+          if (MODE == kModeMain && !SSM_FWD_LATEZ) {   // branch-free: without z the tiles hold zeros
             const float zz = to_f32(Zs[tt * BXC + dl]);
             if (g == tt % LPC) zk[tt / LPC] = zz;
           }
@@ -335,12 +338,19 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
 #pragma unroll
           for (int i = 0; i < NP; ++i) {
             h[i] = fwd_apply2<METHOD>(h[i], av[q][i], bv[q][i]);
-            if (MODE == kModeMain) acc = fma2(cv[q][i], h[i], acc);
+            if (MODE == kModeMain) acc = (SSM_FWD_LATEZ && i == 0) ? mul2(cv[q][i], h[i]) : fma2(cv[q][i], h[i], acc);
             else P[i] = mul2(P[i], av[q][i]);
           }
           yp[(tt % LPC) * YPL + tt / LPC] = acc.x + acc.y;
         }
-        if (SSM_FWD_PIPE && MODE == kModeMain && t0s == (TC > SSM_FWD_SUB ? SSM_FWD_SUB : 0)) emit(ypv, zpv, tpv);
+        if (SSM_FWD_PIPE && MODE == kModeMain && t0s == (TC > SSM_FWD_SUB ? SSM_FWD_SUB : 0)) emit(ypv, zpv, upv, tpv);
+      }
+      if (MODE == kModeMain && SSM_FWD_LATEZ) {   // z and u of the lane's output steps, before the refill
+#pragma unroll
+        for (int i = 0; i < YPL; ++i) {
+          zk[i] = to_f32(Zs[(g + i * LPC) * BXC + dl]);
+          uk[i] = to_f32(Xs[(g + i * LPC) * BXC + dl]);
+        }
       }
     }
     // every lane has read this stage: hand it back to the TMA ring
@@ -353,16 +363,19 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
 #pragma unroll
         for (int i = 0; i < TC; ++i) ypv[i] = yp[i];
 #pragma unroll
-        for (int i = 0; i < YPL; ++i) zpv[i] = zk[i];
+        for (int i = 0; i < YPL; ++i) {
+          zpv[i] = zk[i];
+          upv[i] = uk[i];
+        }
         tpv = t0;
       } else {
-        emit(yp, zk, t0);
+        emit(yp, zk, uk, t0);
       }
     }
   }
 
   if (MODE == kModeMain) {
-    if (SSM_FWD_PIPE) emit(ypv, zpv, tpv);
+    if (SSM_FWD_PIPE) emit(ypv, zpv, upv, tpv);
     if (dvalid && t_end == p.L && p.last != nullptr) storep<G>(p.last + ((size_t)b * p.D + d) * N + nbase, h);
   } else if (dvalid) {
     const size_t o = (((size_t)b * p.nseg + seg) * p.D + d) * N + nbase;
