@@ -12,7 +12,8 @@ value  : whole-job tokens/s with inputs resident in HBM (CUDA events around exac
          that every step touches buffers evicted from the 126 MB L2 (4 sets, ~0.5 GB).
 e2e    : the same metric through the public Python API (selective_scan_fused + autograd
          backward) with host (pinned) inputs and outputs: H2D copies, fwd, bwd and D2H copies
-         of every output inside the timed region.
+         of every output inside the timed region (copies on their own streams, overlapping the
+         neighbouring steps' compute).
 N > 1  : one process per GPU (torchrun).  Channel sharding, weak scaling: every rank owns a
          512-channel shard of a (512 N)-channel layer; B and C are shared, so the backward
          ends with an NCCL all-reduce of dB|dC (the real exchange of channel sharding).
@@ -192,41 +193,69 @@ class ScanStep:
 
 
 def e2e_run(cfg, device, steps, world, seed):
-    """Public API with host buffers: H2D + fwd + bwd + D2H of every output, per step."""
+    """Public API with host buffers: every step copies its inputs from pinned host memory, runs the
+    forward and backward through selective_scan_fused + autograd, and copies every output back to
+    pinned host memory.  The copies run on their own streams with double-buffered device inputs, so
+    step i's device-to-host copy and step i+1's host-to-device copy overlap step i's compute."""
     from mamba_ssm_benchmark_b200 import selective_scan_fused, sharding
     from mamba_ssm_benchmark_b200.workloads import make_inputs
     ins = make_inputs(cfg.B, cfg.L, cfg.D, cfg.N, seed=seed, dist="config", dtype=cfg.dtype)
     host = {k: v.pin_memory() for k, v in ins.items() if v is not None}
     h2d = sum(v.numel() * v.element_size() for v in host.values())
-    outs_host = None
-    stream = torch.cuda.current_stream(device)
+    compute = torch.cuda.current_stream(device)
+    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    dev_sets = [{k: torch.empty(v.shape, dtype=v.dtype, device=device) for k, v in host.items()} for _ in range(2)]
+    up_done = [torch.cuda.Event() for _ in range(2)]
+    comp_done = [torch.cuda.Event() for _ in range(2)]
+    outs_host = [None, None]
+    d2h = 0
 
-    def step():
-        nonlocal outs_host
-        dv = {k: v.to(device, non_blocking=True) for k, v in host.items()}
-        leaves = [dv[k].requires_grad_() for k in ("u", "delta", "A", "Bm", "Cm", "Dskip", "z")]
+    def upload(k):
+        up.wait_event(comp_done[k])               # the compute that last read this set is done
+        with torch.cuda.stream(up):
+            for n, v in host.items():
+                dev_sets[k][n].copy_(v, non_blocking=True)
+        up_done[k].record(up)
+
+    def compute_step(k):
+        nonlocal d2h
+        compute.wait_event(up_done[k])
+        dv = dev_sets[k]
+        leaves = [dv[n].detach().requires_grad_() for n in ("u", "delta", "A", "Bm", "Cm", "Dskip", "z")]
         y, last = selective_scan_fused(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4], D=leaves[5],
                                        z=leaves[6])
         grads = list(torch.autograd.grad(y, leaves, dv["dy"]))
         if world > 1:
             sharding.reduce_shared_grads(grads[3:5])          # dBm, dCm: partial sums over channel shards
         res = [y.detach(), last.detach()] + grads
-        if outs_host is None:
-            outs_host = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
-        for o, r in zip(outs_host, res):
-            o.copy_(r, non_blocking=True)
-        return sum(r.numel() * r.element_size() for r in res)
+        comp_done[k].record(compute)
+        if outs_host[k] is None:
+            outs_host[k] = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+        down.wait_event(comp_done[k])
+        with torch.cuda.stream(down):
+            for o, r in zip(outs_host[k], res):
+                o.copy_(r, non_blocking=True)
+                r.record_stream(down)
+        d2h = sum(r.numel() * r.element_size() for r in res)
 
-    for _ in range(3):
-        d2h = step()
+    def run(n):
+        upload(0)
+        for i in range(n):
+            k = i % 2
+            if i + 1 < n:
+                upload(1 - k)
+            compute_step(k)
+        compute.wait_stream(up)
+        compute.wait_stream(down)
+
+    run(3)
     torch.cuda.synchronize(device)
     if world > 1:
         torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        step()
-    e1.record(stream)
+    e0.record(compute)
+    run(steps)
+    e1.record(compute)
     torch.cuda.synchronize(device)
     ms = e0.elapsed_time(e1)
     if world > 1:

@@ -53,12 +53,20 @@ struct FwdSmem {
 // h' = a (h + g) - g with g = B u / A; the coefficient kept is ng = -g (so both uses are one
 // packed FMA): h + g = fma(ng, -1, h), h' = fma(a, h + g, ng).  Euler and bilinear use
 // h' = a h + b.
+#ifndef SSM_CHAIN1
+// 1: the forward's ZOH recurrence runs as h' = a h + b with b = g (1 - a), g = -B u / A, formed in
+// phase A (one FMA per step on the dependency chain); 0: h' = a (h - g) + g in phase B (two).
+// (The backward's recompute keeps the second form: measured faster there.)
+#define SSM_CHAIN1 1
+#endif
+
 template <int METHOD>
 __device__ __forceinline__ void fwd_coeffs2(float2 dt2, float2 u2, float2 dtu2, float2 B2, float2 Ak2, float2 A2k2,
                                             float2 niA2, float2& a, float2& bco) {
   if (METHOD == kZOH) {
     a = ex2x2(mul2(dt2, A2k2));
     bco = mul2(mul2(B2, u2), niA2);
+    if (SSM_CHAIN1) bco = fma2(bco, make_float2(-a.x, -a.y), bco);
   } else if (METHOD == kEuler) {
     a = ex2x2(mul2(dt2, A2k2));
     bco = mul2(dtu2, B2);
@@ -71,7 +79,7 @@ __device__ __forceinline__ void fwd_coeffs2(float2 dt2, float2 u2, float2 dtu2, 
 }
 template <int METHOD>
 __device__ __forceinline__ float2 fwd_apply2(float2 h, float2 a, float2 bco) {
-  if (METHOD == kZOH) return fma2(a, fma2(bco, bc2(-1.0f), h), bco);
+  if (METHOD == kZOH && !SSM_CHAIN1) return fma2(a, fma2(bco, bc2(-1.0f), h), bco);
   return fma2(a, h, bco);
 }
 
