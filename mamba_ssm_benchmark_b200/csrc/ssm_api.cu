@@ -291,25 +291,29 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   bool use_tma = tma_ok(u, B, L, D) && tma_ok(delta, B, L, D) && tma_ok(Bm, B, L, N);
   if (!summary) use_tma = use_tma && tma_ok(Cm, B, L, N);
   if (phase != 1) use_tma = use_tma && (!p.has_z || tma_ok(z, B, L, D));
-  if (use_tma) {
-    bool ok = make_map(&p.tm_u, u, B, L, D, bxc, kChunk) && make_map(&p.tm_dt, delta, B, L, D, bxc, kChunk) &&
-              make_map(&p.tm_B, Bm, B, L, N, (int)N, kChunk);
-    if (!summary) ok = ok && make_map(&p.tm_C, Cm, B, L, N, (int)N, kChunk);
-    if (phase != 1 && p.has_z) ok = ok && make_map(&p.tm_z, z, B, L, D, bxc, kChunk);
-    use_tma = ok;
-  }
-  p.use_tma = use_tma ? 1 : 0;
-
   int S, len;
   plan_segments(B, L, D, N, &S, &len);
   p.nseg = S;
   p.seg_len = len;
+  // TMA boxes of kb 16-step tiles: 4 for an unsplit main pass whose warps all fit at once with the
+  // larger ring (fp32: 8 per SM), else 2 (split sequences with short segments, summary passes)
+  const int64_t fwd_warps = B * ((D + cpw - 1) / cpw);
+  const int kb = (S == 1 && !summary && (dt == SSM_BF16 || fwd_warps <= 8 * (int64_t)sm_count())) ? 4 : 2;
+  if (use_tma) {
+    const int rows = kChunk * kb;
+    bool ok = make_map(&p.tm_u, u, B, L, D, bxc, rows) && make_map(&p.tm_dt, delta, B, L, D, bxc, rows) &&
+              make_map(&p.tm_B, Bm, B, L, N, (int)N, rows);
+    if (!summary) ok = ok && make_map(&p.tm_C, Cm, B, L, N, (int)N, rows);
+    if (phase != 1 && p.has_z) ok = ok && make_map(&p.tm_z, z, B, L, D, bxc, rows);
+    use_tma = ok;
+  }
+  p.use_tma = use_tma ? 1 : 0;
   const unsigned ndt = (unsigned)((D + 31) / 32);
   const dim3 grid(ndt, (unsigned)S, (unsigned)B);
   const bool bf = dt == SSM_BF16;
   auto launch = [&](int mode, const FwdParams& q) {
-    return bf ? launch_fwd<__nv_bfloat16>((int)N, G, method, mode, q, grid, stream)
-              : launch_fwd<float>((int)N, G, method, mode, q, grid, stream);
+    return bf ? launch_fwd<__nv_bfloat16>((int)N, G, method, mode, kb, q, grid, stream)
+              : launch_fwd<float>((int)N, G, method, mode, kb, q, grid, stream);
   };
   cudaError_t e;
 

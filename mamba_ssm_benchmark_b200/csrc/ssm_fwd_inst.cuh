@@ -5,10 +5,10 @@
 
 namespace ssm {
 
-template <typename T, int N, int G, int METHOD, int MODE>
+template <typename T, int N, int G, int METHOD, int MODE, int KB>
 static cudaError_t launch_fwd_nm(const FwdParams& p, dim3 grid, cudaStream_t stream) {
-  auto kern = ssm_fwd_kernel<N, G, METHOD, T, MODE>;
-  constexpr int smem = FwdSmem<N, G, T>::BYTES;
+  auto kern = ssm_fwd_kernel<N, G, METHOD, T, MODE, KB>;
+  constexpr int smem = FwdSmem<N, G, T, KB>::BYTES;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -20,47 +20,45 @@ static cudaError_t launch_fwd_nm(const FwdParams& p, dim3 grid, cudaStream_t str
   return cudaGetLastError();
 }
 
-template <typename T, int N, int G>
-static cudaError_t launch_fwd_n(int method, int mode, const FwdParams& p, dim3 grid, cudaStream_t stream) {
-  if (mode == kModeMain) {
-    switch (method) {
-      case kZOH: return launch_fwd_nm<T, N, G, kZOH, kModeMain>(p, grid, stream);
-      case kEuler: return launch_fwd_nm<T, N, G, kEuler, kModeMain>(p, grid, stream);
-      case kBilinear: return launch_fwd_nm<T, N, G, kBilinear, kModeMain>(p, grid, stream);
-    }
-  } else if (mode == kModeSummary) {
-    switch (method) {
-      case kZOH: return launch_fwd_nm<T, N, G, kZOH, kModeSummary>(p, grid, stream);
-      case kEuler: return launch_fwd_nm<T, N, G, kEuler, kModeSummary>(p, grid, stream);
-      case kBilinear: return launch_fwd_nm<T, N, G, kBilinear, kModeSummary>(p, grid, stream);
-    }
-  } else if (mode == kModeAdjoint) {
-    switch (method) {
-      case kZOH: return launch_fwd_nm<T, N, G, kZOH, kModeAdjoint>(p, grid, stream);
-      case kEuler: return launch_fwd_nm<T, N, G, kEuler, kModeAdjoint>(p, grid, stream);
-      case kBilinear: return launch_fwd_nm<T, N, G, kBilinear, kModeAdjoint>(p, grid, stream);
-    }
+template <typename T, int N, int G, int MODE, int KB>
+static cudaError_t launch_fwd_m(int method, const FwdParams& p, dim3 grid, cudaStream_t stream) {
+  switch (method) {
+    case kZOH: return launch_fwd_nm<T, N, G, kZOH, MODE, KB>(p, grid, stream);
+    case kEuler: return launch_fwd_nm<T, N, G, kEuler, MODE, KB>(p, grid, stream);
+    case kBilinear: return launch_fwd_nm<T, N, G, kBilinear, MODE, KB>(p, grid, stream);
   }
+  return cudaErrorInvalidValue;
+}
+
+// The main pass exists with 2- and 4-tile boxes; the summary and adjoint passes (split sequences,
+// short segments) use 2-tile boxes.
+template <typename T, int N, int G>
+static cudaError_t launch_fwd_n(int method, int mode, int kb, const FwdParams& p, dim3 grid, cudaStream_t stream) {
+  if (mode == kModeMain)
+    return kb == 4 ? launch_fwd_m<T, N, G, kModeMain, 4>(method, p, grid, stream)
+                   : launch_fwd_m<T, N, G, kModeMain, 2>(method, p, grid, stream);
+  if (mode == kModeSummary) return launch_fwd_m<T, N, G, kModeSummary, 2>(method, p, grid, stream);
+  if (mode == kModeAdjoint) return launch_fwd_m<T, N, G, kModeAdjoint, 2>(method, p, grid, stream);
   return cudaErrorInvalidValue;
 }
 
 // G = 2 (twice the threads for small grids) is built for N = 8 and 16.
 template <>
-cudaError_t launch_fwd<SSM_ELEM>(int N, int G, int method, int mode, const FwdParams& p, dim3 grid,
+cudaError_t launch_fwd<SSM_ELEM>(int N, int G, int method, int mode, int kb, const FwdParams& p, dim3 grid,
                                  cudaStream_t stream) {
   if (G == 2) {
     switch (N) {
-      case 8: return launch_fwd_n<SSM_ELEM, 8, 2>(method, mode, p, grid, stream);
-      case 16: return launch_fwd_n<SSM_ELEM, 16, 2>(method, mode, p, grid, stream);
+      case 8: return launch_fwd_n<SSM_ELEM, 8, 2>(method, mode, kb, p, grid, stream);
+      case 16: return launch_fwd_n<SSM_ELEM, 16, 2>(method, mode, kb, p, grid, stream);
     }
     return cudaErrorInvalidValue;
   }
   switch (N) {
-    case 4: return launch_fwd_n<SSM_ELEM, 4, 4>(method, mode, p, grid, stream);
-    case 8: return launch_fwd_n<SSM_ELEM, 8, 4>(method, mode, p, grid, stream);
-    case 16: return launch_fwd_n<SSM_ELEM, 16, 4>(method, mode, p, grid, stream);
-    case 32: return launch_fwd_n<SSM_ELEM, 32, 4>(method, mode, p, grid, stream);
-    case 64: return launch_fwd_n<SSM_ELEM, 64, 4>(method, mode, p, grid, stream);
+    case 4: return launch_fwd_n<SSM_ELEM, 4, 4>(method, mode, kb, p, grid, stream);
+    case 8: return launch_fwd_n<SSM_ELEM, 8, 4>(method, mode, kb, p, grid, stream);
+    case 16: return launch_fwd_n<SSM_ELEM, 16, 4>(method, mode, kb, p, grid, stream);
+    case 32: return launch_fwd_n<SSM_ELEM, 32, 4>(method, mode, kb, p, grid, stream);
+    case 64: return launch_fwd_n<SSM_ELEM, 64, 4>(method, mode, kb, p, grid, stream);
   }
   return cudaErrorInvalidValue;
 }
