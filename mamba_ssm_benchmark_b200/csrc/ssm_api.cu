@@ -295,10 +295,14 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   plan_segments(B, L, D, N, &S, &len);
   p.nseg = S;
   p.seg_len = len;
-  // TMA boxes of kb 16-step tiles: 4 for an unsplit main pass whose warps all fit at once with the
-  // larger ring (fp32: 8 per SM), else 2 (split sequences with short segments, summary passes)
+  // TMA boxes of kb 16-step tiles: 4 for an unsplit main pass whose warps (one per CTA) all fit on
+  // the GPU at once with the larger ring's shared memory, else 2 (split sequences with short
+  // segments, summary passes, grids that would need extra waves)
+  const bool bf = dt == SSM_BF16;
   const int64_t fwd_warps = B * ((D + cpw - 1) / cpw);
-  const int kb = (S == 1 && !summary && (dt == SSM_BF16 || fwd_warps <= 8 * (int64_t)sm_count())) ? 4 : 2;
+  const int smem4 = bf ? fwd_smem_bytes<__nv_bfloat16>((int)N, G, 4) : fwd_smem_bytes<float>((int)N, G, 4);
+  const int64_t ctas4 = std::min<int64_t>(32, (228 * 1024) / (smem4 + 1024));   // per SM
+  const int kb = (S == 1 && !summary && fwd_warps <= ctas4 * (int64_t)sm_count()) ? 4 : 2;
   if (use_tma) {
     const int rows = kChunk * kb;
     bool ok = make_map(&p.tm_u, u, B, L, D, bxc, rows) && make_map(&p.tm_dt, delta, B, L, D, bxc, rows) &&
@@ -310,7 +314,6 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   p.use_tma = use_tma ? 1 : 0;
   const unsigned ndt = (unsigned)((D + 31) / 32);
   const dim3 grid(ndt, (unsigned)S, (unsigned)B);
-  const bool bf = dt == SSM_BF16;
   auto launch = [&](int mode, const FwdParams& q) {
     return bf ? launch_fwd<__nv_bfloat16>((int)N, G, method, mode, kb, q, grid, stream)
               : launch_fwd<float>((int)N, G, method, mode, kb, q, grid, stream);

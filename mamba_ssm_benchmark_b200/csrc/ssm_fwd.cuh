@@ -411,5 +411,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
 // Host-side launcher (defined per element type in ssm_fwd_<type>.cu).  G = states per thread.
 template <typename T>
 cudaError_t launch_fwd(int N, int G, int method, int mode, int kb, const FwdParams& p, dim3 grid, cudaStream_t stream);
+template <typename T>
+int fwd_smem_bytes(int N, int G, int kb);
 
 }  // namespace ssm

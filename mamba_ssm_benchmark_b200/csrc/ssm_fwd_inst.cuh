@@ -1,6 +1,8 @@
 // ssm_fwd_inst.cuh — instantiates and dispatches the forward kernels for one element type
 // (SSM_ELEM, set by the including translation unit).
 #pragma once
+#include <type_traits>
+
 #include "ssm_fwd.cuh"
 
 namespace ssm {
@@ -61,6 +63,25 @@ cudaError_t launch_fwd<SSM_ELEM>(int N, int G, int method, int mode, int kb, con
     case 64: return launch_fwd_n<SSM_ELEM, 64, 4>(method, mode, kb, p, grid, stream);
   }
   return cudaErrorInvalidValue;
+}
+
+// Dynamic shared memory of one forward CTA (one warp) with KB-tile boxes.
+template <>
+int fwd_smem_bytes<SSM_ELEM>(int N, int G, int kb) {
+  auto pick = [&](auto n_const, auto g_const) {
+    constexpr int NN = decltype(n_const)::value, GG = decltype(g_const)::value;
+    return kb == 4 ? FwdSmem<NN, GG, SSM_ELEM, 4>::BYTES : FwdSmem<NN, GG, SSM_ELEM, 2>::BYTES;
+  };
+  using I4 = std::integral_constant<int, 4>;
+  using I2 = std::integral_constant<int, 2>;
+  if (G == 2) return N == 8 ? pick(std::integral_constant<int, 8>{}, I2{}) : pick(std::integral_constant<int, 16>{}, I2{});
+  switch (N) {
+    case 4: return pick(std::integral_constant<int, 4>{}, I4{});
+    case 8: return pick(std::integral_constant<int, 8>{}, I4{});
+    case 16: return pick(std::integral_constant<int, 16>{}, I4{});
+    case 32: return pick(std::integral_constant<int, 32>{}, I4{});
+    default: return pick(std::integral_constant<int, 64>{}, I4{});
+  }
 }
 
 }  // namespace ssm
