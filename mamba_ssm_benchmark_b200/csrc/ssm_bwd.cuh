@@ -65,11 +65,10 @@ struct BwdSmem {
   static constexpr int OP = PadPitch<Gm::CPW, T>::value;
   static constexpr int OPF = PadPitch<Gm::CPW, float>::value;
   static constexpr int OUT = ((TC * OP * (int)sizeof(T)) + 127) / 128 * 128;
-  static constexpr int OFF_DYS = NSTAGE * STAGE;               // dy * silu(z), fp32, padded
-  static constexpr int FT = ((TC * OPF * 4 + 127) / 128) * 128;   // one padded (16 x DT) fp32 tile
-  static constexpr int OFF_SDT = OFF_DYS + FT;                 // dt_softplus: delta = softplus(raw + bias)
-  static constexpr int OFF_SSG = OFF_SDT + FT;                 // dt_softplus: sigmoid(raw + bias)
-  static constexpr int OFF_BP = OFF_SSG + FT;                  // G perms x (16 x N) fp32 B
+  // per (t, d) of the chunk, packed for one 128-bit load per step: {u, delta (activated when
+  // dt_softplus), dy silu(z), sigmoid(raw delta + bias) (dt_softplus)}
+  static constexpr int OFF_SUD = NSTAGE * STAGE;
+  static constexpr int OFF_BP = OFF_SUD + TC * DT * 16;        // G perms x (16 x N) fp32 B
   static constexpr int OFF_CP = OFF_BP + G * TC * N * 4;       // G perms x (16 x N) fp32 C
   // Either the recomputed states (HSMEM) or the decays (ACACHE) are kept in shared memory;
   // the other lives in registers / is recomputed.
@@ -149,9 +148,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
   constexpr int QDUP = (LPC > QV) ? LPC / QV : 1;      // lanes holding the same value
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
-  float* __restrict__ SDYS = reinterpret_cast<float*>(smem + S::OFF_DYS);
-  float* __restrict__ SDT = reinterpret_cast<float*>(smem + S::OFF_SDT);
-  float* __restrict__ SSG = reinterpret_cast<float*>(smem + S::OFF_SSG);
+  float4* __restrict__ SUD = reinterpret_cast<float4*>(smem + S::OFF_SUD);
   float* __restrict__ SBP = reinterpret_cast<float*>(smem + S::OFF_BP);
   float* __restrict__ SCP = reinterpret_cast<float*>(smem + S::OFF_CP);
   float* __restrict__ SAC = reinterpret_cast<float*>(smem + S::OFF_AC);
@@ -254,7 +251,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
       const T* DYs = reinterpret_cast<const T*>(st + S::OFF_DY);
       const T* YGs = reinterpret_cast<const T*>(st + S::OFF_YG);
       for (int e = tid; e < TC * DT; e += NT) {
-        const int ep = (e / DT) * OP + (e % DT), epf = (e / DT) * OPF + (e % DT);
+        const int ep = (e / DT) * OP + (e % DT);
         const float dyv = to_f32(DYs[e]);
         const float uu = to_f32(Xs[e]);
         float dys = dyv;
@@ -264,14 +261,15 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
           dys = dyv * zz * sg;
           DZo[ep] = from_f32<T>(dyv * to_f32(YGs[e]) * sg * fmaf(zz, 1.0f - sg, 1.0f));
         }
-        SDYS[epf] = dys;
         dDacc = fmaf(dys, uu, dDacc);   // thread tid always sees channel tid % 32
+        float dtv = to_f32(DLs[e]), sgd = 0.0f;
         if (p.dt_softplus) {            // rows past L keep delta = 0 (identity steps)
-          const float xr = to_f32(DLs[e]) + dtb_gate;
+          const float xr = dtv + dtb_gate;
           const bool in = t0 + e / DT < p.L;
-          SDT[epf] = in ? softplus(xr) : 0.0f;
-          SSG[epf] = in ? sigmoid(xr) : 0.0f;
+          dtv = in ? softplus(xr) : 0.0f;
+          sgd = in ? sigmoid(xr) : 0.0f;
         }
+        SUD[e] = make_float4(uu, dtv, dys, sgd);
       }
       const T* Bs = reinterpret_cast<const T*>(st + S::OFF_B);
       const T* Cs = reinterpret_cast<const T*>(st + S::OFF_C);
@@ -302,8 +300,8 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
       for (int k = 0; k < NP; ++k) hc[k] = hs[k];
 #pragma unroll
       for (int j = 0; j < TC; ++j) {
-        const float uu = to_f32(Xs[j * DT + dl]);
-        const float dtv = p.dt_softplus ? SDT[j * OPF + dl] : to_f32(DLs[j * DT + dl]);
+        const float4 q4 = SUD[j * DT + dl];
+        const float uu = q4.x, dtv = q4.y;
         const float2 u2 = bc2(uu), dt2 = bc2(dtv), dtu2 = bc2(dtv * uu);
         float2 Bn[NP], av[NP];
         loadp<G>(Bp + j * N, Bn);
@@ -335,19 +333,31 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
     // which turns every per-state update into one packed FMA.
     float2 hnext[NP];            // HSMEM: state of step j, carried from step j + 1's load
     if (S::HSMEM) loadp<G>(Acache + (TC - 1) * NT * G, hnext);
+    float4 qn = SUD[(TC - 1) * DT + dl];   // the last step's inputs, prefetched
+    float2 Bnn[NP], Cnn[NP];
+    loadp<G>(Bp + (TC - 1) * N, Bnn);
+    loadp<G>(Cp + (TC - 1) * N, Cnn);
 #pragma unroll
     for (int jg = TC / 4 - 1; jg >= 0; --jg) {
       float red[QV];
 #pragma unroll
       for (int jj = 3; jj >= 0; --jj) {
         const int j = jg * 4 + jj;
-        const float uu = to_f32(Xs[j * DT + dl]);
-        const float dtv = p.dt_softplus ? SDT[j * OPF + dl] : to_f32(DLs[j * DT + dl]);
-        const float dys = SDYS[j * OPF + dl];
-        const float2 u2 = bc2(uu), dt2 = bc2(dtv), dys2 = bc2(dys);
+        // step j's inputs were fetched one step ahead; fetch step j - 1's now
+        const float4 q4 = qn;
         float2 Bn[NP], Cn[NP], av[NP], hprev[NP];
-        loadp<G>(Bp + j * N, Bn);
-        loadp<G>(Cp + j * N, Cn);
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+          Bn[k] = Bnn[k];
+          Cn[k] = Cnn[k];
+        }
+        if (j > 0) {
+          qn = SUD[(j - 1) * DT + dl];
+          loadp<G>(Bp + (j - 1) * N, Bnn);
+          loadp<G>(Cp + (j - 1) * N, Cnn);
+        }
+        const float uu = q4.x, dtv = q4.y, dys = q4.z;
+        const float2 u2 = bc2(uu), dt2 = bc2(dtv), dys2 = bc2(dys);
         if (S::ACACHE) {
           loadp<G>(Acache + j * NT * G, av);
         } else {
@@ -473,12 +483,12 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
           if (idx & 1) {
             float g = red[v];
             if (p.dt_softplus) {      // chain rule through softplus(raw + bias)
-              g *= SSG[j * OPF + dl];
+              g *= SUD[j * DT + dl].w;
               dtbacc += g;
             }
             DDTo[j * OP + dl] = from_f32<T>(g);
           } else {
-            DUo[j * OP + dl] = from_f32<T>(fmaf(Dd, SDYS[j * OPF + dl], red[v]));
+            DUo[j * OP + dl] = from_f32<T>(fmaf(Dd, SUD[j * DT + dl].z, red[v]));
           }
         }
       }
