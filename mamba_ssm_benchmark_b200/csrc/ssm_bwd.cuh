@@ -298,13 +298,21 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
       float2 hc[NP];
 #pragma unroll
       for (int k = 0; k < NP; ++k) hc[k] = hs[k];
+      float4 rq = SUD[dl];                 // step 0's inputs; each step fetches the next one's
+      float2 rB[NP];
+      loadp<G>(Bp, rB);
 #pragma unroll
       for (int j = 0; j < TC; ++j) {
-        const float4 q4 = SUD[j * DT + dl];
+        const float4 q4 = rq;
+        float2 Bn[NP], av[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) Bn[k] = rB[k];
+        if (j + 1 < TC) {
+          rq = SUD[(j + 1) * DT + dl];
+          loadp<G>(Bp + (j + 1) * N, rB);
+        }
         const float uu = q4.x, dtv = q4.y;
         const float2 u2 = bc2(uu), dt2 = bc2(dtv), dtu2 = bc2(dtv * uu);
-        float2 Bn[NP], av[NP];
-        loadp<G>(Bp + j * N, Bn);
 #pragma unroll
         for (int k = 0; k < NP; ++k) {
           if (METHOD == kZOH) {

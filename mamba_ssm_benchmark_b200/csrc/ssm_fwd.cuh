@@ -289,6 +289,16 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
       }
       __syncwarp();
     }
+    // the step sizes this tile reads: the activated tile, or the raw box (fp32: one pointer, chosen
+    // once per tile, so the unrolled step loop stays one basic block)
+    const float* const dsrc = (sizeof(T) == 4 && !p.dt_softplus) ? reinterpret_cast<const float*>(DLs) : SDT;
+    auto delta_at = [&](int i) -> float {
+      if constexpr (sizeof(T) == 4) {
+        return dsrc[i];
+      } else {
+        return p.dt_softplus ? SDT[i] : to_f32(DLs[i]);
+      }
+    };
 
     float yp[TC], zk[YPL], uk[YPL];   // main mode: partial y; the gate's z and the D-skip u of the lane's output steps
     if constexpr (MODE == kModeAdjoint) {
@@ -300,8 +310,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
         for (int q = 0; q < SSM_FWD_SUB; ++q) {
           const int tt = t0s + q;
           float dys = to_f32(Xs[tt * BXC + dl]);
-          float dtv = to_f32(DLs[tt * BXC + dl]);
-          if (p.dt_softplus) dtv = SDT[tt * BXC + dl];
+          const float dtv = delta_at(tt * BXC + dl);
           if (p.has_z) {
             const float zz = to_f32(Zs[tt * BXC + dl]);
             dys *= zz * sigmoid(zz);
@@ -339,8 +348,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
         for (int q = 0; q < SSM_FWD_SUB; ++q) {
           const int tt = t0s + q;
           const float uu = to_f32(Xs[tt * BXC + dl]);
-          float dtv = to_f32(DLs[tt * BXC + dl]);
-          if (p.dt_softplus) dtv = SDT[tt * BXC + dl];
+          const float dtv = delta_at(tt * BXC + dl);
           const float2 u2 = bc2(uu), dt2 = bc2(dtv), dtu2 = bc2(dtv * uu);
           float2 Bn[NP];
           loadp<G>(Bs + tt * N + nbase, Bn);
