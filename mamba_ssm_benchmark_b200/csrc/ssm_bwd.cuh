@@ -250,7 +250,10 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
       const T* Zs = reinterpret_cast<const T*>(st + S::OFF_Z);
       const T* DYs = reinterpret_cast<const T*>(st + S::OFF_DY);
       const T* YGs = reinterpret_cast<const T*>(st + S::OFF_YG);
-      for (int e = tid; e < TC * DT; e += NT) {
+      static_assert((TC * DT) % NT == 0, "the gate pass gives every thread the same number of elements");
+#pragma unroll
+      for (int k = 0; k < TC * DT / NT; ++k) {   // a fixed trip count lets the loads be issued together
+        const int e = tid + k * NT;
         const int ep = (e / DT) * OP + (e % DT);
         const float dyv = to_f32(DYs[e]);
         const float uu = to_f32(Xs[e]);
@@ -504,8 +507,11 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
 
     __syncthreads();
 
-    // cross-warp dB | dC sum -> this CTA's partial (fixed order)
-    for (int e = tid; e < TC * 2 * N; e += NT) {
+    // cross-warp dB | dC sum -> this CTA's partial (fixed order); TC * 2N = G * NT elements
+    static_assert(TC * 2 * N == G * NT, "every thread sums G of the chunk's dB | dC values");
+#pragma unroll
+    for (int k = 0; k < G; ++k) {
+      const int e = tid + k * NT;
       const int j = e / (2 * N), v = e % (2 * N);
       float sum = 0.f;
 #pragma unroll
@@ -549,67 +555,53 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
   }
 }
 
-// Sums the per-CTA dB | dC partials over channel tiles and the dA / dD partials over batch,
-// each in a fixed order, and writes dB, dC (element type T), dA, dD (fp32).
+// Sums the per-CTA dB | dC partials over channel tiles and the dA / dD / step-size-bias partials
+// over batch, each in a fixed order (loads of a group of kU terms are issued together, then added in
+// index order), and writes dB, dC (element type T), dA, dD, d(bias) (fp32).  dB | dC: one warp per
+// (b, t) row, lanes over its 2N values (coalesced, one index division per row); the rest: one
+// thread per output.
 template <typename T>
 __global__ void ssm_bwd_finalize(const FinParams p) {
-  // Each sum is taken in index order; the loads of a group of kU terms are issued together
-  // (they are independent), then added in order, so the result does not depend on kU.
   constexpr int kU = 8;
-  const long long n2 = 2LL * p.N;
-  const long long nbc = (long long)p.B * p.L * n2;
-  const long long nA = (long long)p.D * p.N;
-  const long long nDD = p.dD != nullptr ? p.D : 0;
-  const long long total = nbc + nA + nDD + (p.ddt_bias != nullptr ? p.D : 0);
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const float* src;
-    long long stride;
-    int cnt;
-    if (idx < nbc) {
-      const int v = (int)(idx % n2);
-      const long long bt = idx / n2;
-      const int t = (int)(bt % p.L), b = (int)(bt / p.L);
-      src = p.part_bc + ((size_t)b * p.ndt * p.L + t) * n2 + v;
-      stride = (long long)p.L * n2;
-      cnt = p.ndt;
-    } else if (idx < nbc + nA) {
-      src = p.part_A + (idx - nbc);
-      stride = nA;
-      cnt = p.B;
-    } else if (idx < nbc + nA + nDD) {
-      src = p.part_D + (idx - nbc - nA);
-      stride = p.D;
-      cnt = p.B;
-    } else {
-      src = p.part_dtb + (idx - nbc - nA - nDD);
-      stride = p.D;
-      cnt = p.B;
-    }
+  auto sum = [&](const float* src, size_t stride, int cnt) {
     float s = 0.f;
     for (int q0 = 0; q0 < cnt; q0 += kU) {
       float v[kU];
 #pragma unroll
-      for (int k = 0; k < kU; ++k) v[k] = (q0 + k < cnt) ? __ldg(src + (q0 + k) * stride) : 0.f;
+      for (int k = 0; k < kU; ++k) v[k] = (q0 + k < cnt) ? __ldg(src + (size_t)(q0 + k) * stride) : 0.f;
 #pragma unroll
       for (int k = 0; k < kU; ++k) s += v[k];
     }
-    if (idx < nbc) {
-      const int v = (int)(idx % n2);
-      const long long bt = idx / n2;
-      const int t = (int)(bt % p.L), b = (int)(bt / p.L);
+    return s;
+  };
+  const int lane = threadIdx.x & 31;
+  const long long gtid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  const long long nthr = (long long)gridDim.x * blockDim.x;
+  const int n2 = 2 * p.N;
+  const long long rows = (long long)p.B * p.L;
+  for (long long r = gtid >> 5; r < rows; r += nthr >> 5) {
+    const int b = (int)(r / p.L), t = (int)(r - (long long)b * p.L);
+    const float* src = p.part_bc + ((size_t)b * p.ndt * p.L + t) * n2;
+    for (int v = lane; v < n2; v += 32) {
+      const float s = sum(src + v, (size_t)p.L * n2, p.ndt);
       if (v < p.N) {
         static_cast<T*>(const_cast<void*>(p.dB.ptr))[b * p.dB.sb + (long long)t * p.dB.sl + v] = from_f32<T>(s);
       } else {
         static_cast<T*>(const_cast<void*>(p.dC.ptr))[b * p.dC.sb + (long long)t * p.dC.sl + (v - p.N)] =
             from_f32<T>(s);
       }
-    } else if (idx < nbc + nA) {
-      p.dA[idx - nbc] = s;
-    } else if (idx < nbc + nA + nDD) {
-      p.dD[idx - nbc - nA] = s;
+    }
+  }
+  const long long nA = (long long)p.D * p.N;
+  const long long nDD = p.dD != nullptr ? p.D : 0;
+  const long long total = nA + nDD + (p.ddt_bias != nullptr ? p.D : 0);
+  for (long long i = gtid; i < total; i += nthr) {
+    if (i < nA) {
+      p.dA[i] = sum(p.part_A + i, (size_t)nA, p.B);
+    } else if (i < nA + nDD) {
+      p.dD[i - nA] = sum(p.part_D + (i - nA), (size_t)p.D, p.B);
     } else {
-      p.ddt_bias[idx - nbc - nA - nDD] = s;
+      p.ddt_bias[i - nA - nDD] = sum(p.part_dtb + (i - nA - nDD), (size_t)p.D, p.B);
     }
   }
 }

@@ -49,8 +49,11 @@ cudaError_t launch_bwd<SSM_ELEM>(int N, int G, int method, const BwdParams& p, d
 
 template <>
 cudaError_t launch_bwd_finalize<SSM_ELEM>(const FinParams& p, cudaStream_t stream) {
-  const long long total = (long long)p.B * p.L * 2 * p.N + (long long)p.D * p.N + 2LL * p.D;
-  long long blocks = (total + 255) / 256;
+  // 8 warps per block, one (b, t) row per warp for dB | dC (grid-stride beyond 16 blocks per SM)
+  const long long rows = (long long)p.B * p.L;
+  long long blocks = (rows + 7) / 8;
+  const long long rest = ((long long)p.D * p.N + 2LL * p.D + 255) / 256;
+  if (blocks < rest) blocks = rest;
   if (blocks > 148 * 16) blocks = 148 * 16;
   ssm_bwd_finalize<SSM_ELEM><<<(unsigned)blocks, 256, 0, stream>>>(p);
   return cudaGetLastError();
