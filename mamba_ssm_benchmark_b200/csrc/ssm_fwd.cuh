@@ -94,6 +94,9 @@ __device__ __forceinline__ float2 fwd_apply2(float2 h, float2 a, float2 bco) {
 #ifndef SSM_FWD_PIPE
 #define SSM_FWD_PIPE 1   // reduce and store box i's outputs while box i + 1's steps run
 #endif
+#ifndef SSM_FWD_PREF
+#define SSM_FWD_PREF 1   // fetch sub-tile k + 1's inputs before computing sub-tile k
+#endif
 #ifndef SSM_FWD_LATEZ
 #define SSM_FWD_LATEZ 1   // z and the D-skip input are read for the lane's output steps only, at the box end
 #endif
@@ -340,19 +343,40 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
       // holds steps g, g + LPC, ...; the lane also keeps z of those steps.  Steps are processed
       // in sub-tiles: phase A computes what does not depend on the state (decays, inputs, C),
       // phase B is only the recurrence and the y accumulation.
+      // the sub-tile's inputs from shared memory; with SSM_FWD_PREF the next sub-tile's are fetched
+      // before this one's coefficients are computed, so the loads' latency overlaps the work
+      float fu[2][SSM_FWD_SUB], fdt[2][SSM_FWD_SUB];
+      float2 fB[2][SSM_FWD_SUB][NP], fC[2][SSM_FWD_SUB][NP];
+      auto fetch = [&](int slot, int base) {
+#pragma unroll
+        for (int q = 0; q < SSM_FWD_SUB; ++q) {
+          const int tt = base + q;
+          fu[slot][q] = to_f32(Xs[tt * BXC + dl]);
+          fdt[slot][q] = delta_at(tt * BXC + dl);
+          loadp<G>(Bs + tt * N + nbase, fB[slot][q]);
+          if (MODE == kModeMain) loadp<G>(Cs + tt * N + nbase, fC[slot][q]);
+        }
+      };
+      if (SSM_FWD_PREF) fetch(0, 0);
 #pragma unroll
       for (int t0s = 0; t0s < TC; t0s += SSM_FWD_SUB) {
+        const int cur = SSM_FWD_PREF ? (t0s / SSM_FWD_SUB) & 1 : 0;
+        if (!SSM_FWD_PREF) fetch(0, t0s);
+        if (SSM_FWD_PREF && t0s + SSM_FWD_SUB < TC) fetch(cur ^ 1, t0s + SSM_FWD_SUB);
         float2 av[SSM_FWD_SUB][NP], bv[SSM_FWD_SUB][NP], cv[SSM_FWD_SUB][NP];
         float yd[SSM_FWD_SUB];
 #pragma unroll
         for (int q = 0; q < SSM_FWD_SUB; ++q) {
           const int tt = t0s + q;
-          const float uu = to_f32(Xs[tt * BXC + dl]);
-          const float dtv = delta_at(tt * BXC + dl);
+          const float uu = fu[cur][q];
+          const float dtv = fdt[cur][q];
           const float2 u2 = bc2(uu), dt2 = bc2(dtv), dtu2 = bc2(dtv * uu);
           float2 Bn[NP];
-          loadp<G>(Bs + tt * N + nbase, Bn);
-          if (MODE == kModeMain) loadp<G>(Cs + tt * N + nbase, cv[q]);
+#pragma unroll
+          for (int i = 0; i < NP; ++i) {
+            Bn[i] = fB[cur][q][i];
+            cv[q][i] = fC[cur][q][i];
+          }
           yd[q] = SSM_FWD_LATEZ ? 0.0f : Dd0 * uu;
 #pragma unroll
           for (int i = 0; i < NP; ++i)
