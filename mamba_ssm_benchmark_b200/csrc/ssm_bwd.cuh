@@ -40,6 +40,9 @@
 #ifndef SSM_BWD_HSMEM
 #define SSM_BWD_HSMEM 0
 #endif
+#ifndef SSM_BWD_PIPE_BC
+#define SSM_BWD_PIPE_BC 1   // reduce step j's dB | dC after step j - 1's math
+#endif
 #ifndef SSM_BWD_ACACHE
 // 1: keep the recompute's decays in shared memory for the reverse pass; 0: recompute them on the
 // MUFU (measured faster: config 1 backward 144 us instead of 155 us, the shared-memory pipe being
@@ -344,6 +347,61 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
     // which turns every per-state update into one packed FMA.
     float2 hnext[NP];            // HSMEM: state of step j, carried from step j + 1's load
     if (S::HSMEM) loadp<G>(Acache + (TC - 1) * NT * G, hnext);
+    float2 pend_b[NP], pend_c[NP];        // SSM_BWD_PIPE_BC: the previous step's dB | dC values
+    // dB | dC of step js over the warp's channels: slot-splitting stages first (a fixed register
+    // slot is sent on every lane thanks to the state permutation), then one stage that splits
+    // dB from dC, then all-reduce stages for the remaining channel bits.  With SSM_BWD_PIPE_BC
+    // step j's reduction runs after step j - 1's math, so its shuffle latency overlaps work.
+    auto reduce_bc = [&](float2 (&xb)[NP], float2 (&xc)[NP], int js) {
+      if constexpr (G == 4 && LC >= 1) {   // slot bit 1: keep pair 0, receive the partner's pair 1
+        constexpr int m = (CPW / 2) * LPC;
+        xb[0] = add2(xb[0], make_float2(__shfl_xor_sync(0xffffffffu, xb[NP - 1].x, m),
+                                          __shfl_xor_sync(0xffffffffu, xb[NP - 1].y, m)));
+        xc[0] = add2(xc[0], make_float2(__shfl_xor_sync(0xffffffffu, xc[NP - 1].x, m),
+                                        __shfl_xor_sync(0xffffffffu, xc[NP - 1].y, m)));
+      }
+      float keep[BCPL];
+      if constexpr (LC >= LG) {            // slot bit 0: (-dB, dC) of slot 0
+        constexpr int m = (CPW >> LG) * LPC;
+        const float2 t2 = add2(make_float2(xb[0].x, xc[0].x),
+                               make_float2(__shfl_xor_sync(0xffffffffu, xb[0].y, m),
+                                           __shfl_xor_sync(0xffffffffu, xc[0].y, m)));
+        if constexpr (QSTAGE) {
+          constexpr int m3 = (CPW >> (LG + 1)) * LPC;
+          const bool up = (c >> (LC - LG - 1)) & 1;
+          const float send = up ? t2.x : t2.y;
+          float kv = (up ? t2.y : t2.x) + __shfl_xor_sync(0xffffffffu, send, m3);
+#pragma unroll
+          for (int mm = CPW >> (LG + 2); mm >= 1; mm >>= 1) kv += __shfl_xor_sync(0xffffffffu, kv, mm * LPC);
+          keep[0] = kv;
+        } else {
+          keep[0] = t2.x;
+          keep[(1) % BCPL] = t2.y;
+        }
+      } else {                             // CPW = 2, G = 4: slots 0 and 1 remain
+        keep[0] = xb[0].x;
+        keep[1 % BCPL] = xb[0].y;
+        keep[2 % BCPL] = xc[0].x;
+        keep[3 % BCPL] = xc[0].y;
+      }
+      {
+        float* dst = SRED + (js * NW + warp) * 2 * N;
+        if constexpr (QSTAGE) {
+          if ((c & (BCDUP - 1)) == 0) {
+            const int q = (c >> (LC - LG - 1)) & 1;
+            dst[q * N + nbase + perm] = q ? keep[0] : -keep[0];
+          }
+        } else if constexpr (LC == LG) {
+          dst[nbase + perm] = -keep[0];
+          dst[N + nbase + perm] = keep[1 % BCPL];
+        } else {
+          dst[nbase + (0 ^ perm)] = -keep[0];
+          dst[nbase + (1 ^ perm)] = -keep[1 % BCPL];
+          dst[N + nbase + (0 ^ perm)] = keep[2 % BCPL];
+          dst[N + nbase + (1 ^ perm)] = keep[3 % BCPL];
+        }
+      }
+    };
     float4 qn = SUD[(TC - 1) * DT + dl];   // the last step's inputs, prefetched
     float2 Bnn[NP], Cnn[NP];
     loadp<G>(Bp + (TC - 1) * N, Bnn);
@@ -427,56 +485,15 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
             dh[k] = mul2(dh[k], a);
           }
         }
-        // dB | dC over the warp's channels: slot-splitting stages first (a fixed register slot
-        // is sent on every lane thanks to the state permutation), then one stage that splits
-        // dB from dC, then all-reduce stages for the remaining channel bits.
-        if constexpr (G == 4 && LC >= 1) {   // slot bit 1: keep pair 0, receive the partner's pair 1
-          constexpr int m = (CPW / 2) * LPC;
-          bBN[0] = add2(bBN[0], make_float2(__shfl_xor_sync(0xffffffffu, bBN[NP - 1].x, m),
-                                            __shfl_xor_sync(0xffffffffu, bBN[NP - 1].y, m)));
-          bC[0] = add2(bC[0], make_float2(__shfl_xor_sync(0xffffffffu, bC[NP - 1].x, m),
-                                          __shfl_xor_sync(0xffffffffu, bC[NP - 1].y, m)));
-        }
-        float keep[BCPL];
-        if constexpr (LC >= LG) {            // slot bit 0: (-dB, dC) of slot 0
-          constexpr int m = (CPW >> LG) * LPC;
-          const float2 t2 = add2(make_float2(bBN[0].x, bC[0].x),
-                                 make_float2(__shfl_xor_sync(0xffffffffu, bBN[0].y, m),
-                                             __shfl_xor_sync(0xffffffffu, bC[0].y, m)));
-          if constexpr (QSTAGE) {
-            constexpr int m3 = (CPW >> (LG + 1)) * LPC;
-            const bool up = (c >> (LC - LG - 1)) & 1;
-            const float send = up ? t2.x : t2.y;
-            float kv = (up ? t2.y : t2.x) + __shfl_xor_sync(0xffffffffu, send, m3);
+        if (SSM_BWD_PIPE_BC) {
+          if (j < TC - 1) reduce_bc(pend_b, pend_c, j + 1);
 #pragma unroll
-            for (int mm = CPW >> (LG + 2); mm >= 1; mm >>= 1) kv += __shfl_xor_sync(0xffffffffu, kv, mm * LPC);
-            keep[0] = kv;
-          } else {
-            keep[0] = t2.x;
-            keep[(1) % BCPL] = t2.y;
+          for (int k = 0; k < NP; ++k) {
+            pend_b[k] = bBN[k];
+            pend_c[k] = bC[k];
           }
-        } else {                             // CPW = 2, G = 4: slots 0 and 1 remain
-          keep[0] = bBN[0].x;
-          keep[1 % BCPL] = bBN[0].y;
-          keep[2 % BCPL] = bC[0].x;
-          keep[3 % BCPL] = bC[0].y;
-        }
-        {
-          float* dst = SRED + (j * NW + warp) * 2 * N;
-          if constexpr (QSTAGE) {
-            if ((c & (BCDUP - 1)) == 0) {
-              const int q = (c >> (LC - LG - 1)) & 1;
-              dst[q * N + nbase + perm] = q ? keep[0] : -keep[0];
-            }
-          } else if constexpr (LC == LG) {
-            dst[nbase + perm] = -keep[0];
-            dst[N + nbase + perm] = keep[1 % BCPL];
-          } else {
-            dst[nbase + (0 ^ perm)] = -keep[0];
-            dst[nbase + (1 ^ perm)] = -keep[1 % BCPL];
-            dst[N + nbase + (0 ^ perm)] = keep[2 % BCPL];
-            dst[N + nbase + (1 ^ perm)] = keep[3 % BCPL];
-          }
+        } else {
+          reduce_bc(bBN, bC, j);
         }
         red[jj * 2 + 0] = -(duN.x + duN.y);
         red[jj * 2 + 1] = ddt.x + ddt.y;
@@ -505,6 +522,15 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
       }
     }
 
+    if (SSM_BWD_PIPE_BC) {               // step 0's dB | dC
+      float2 nb[NP], nc[NP];
+#pragma unroll
+      for (int k = 0; k < NP; ++k) {
+        nb[k] = pend_b[k];
+        nc[k] = pend_c[k];
+      }
+      reduce_bc(nb, nc, 0);
+    }
     __syncthreads();
 
     // cross-warp dB | dC sum -> this CTA's partial (fixed order); TC * 2N = G * NT elements
