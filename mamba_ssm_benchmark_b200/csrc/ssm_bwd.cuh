@@ -509,11 +509,10 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
           const int idx = (g / QDUP) * QPL + v;   // value index: step jg*4 + idx/2, quantity idx%2
           const int j = jg * 4 + (idx >> 1);
           if (idx & 1) {
-            float g = red[v];
-            if (p.dt_softplus) {      // chain rule through softplus(raw + bias)
-              g *= SUD[j * DT + dl].w;
-              dtbacc += g;
-            }
+            // chain rule through softplus(raw + bias), as selects (no branch in the unrolled loop)
+            const float gs = red[v] * SUD[j * DT + dl].w;
+            const float g = p.dt_softplus ? gs : red[v];
+            dtbacc += p.dt_softplus ? gs : 0.0f;
             DDTo[j * OP + dl] = from_f32<T>(g);
           } else {
             DUo[j * OP + dl] = from_f32<T>(fmaf(Dd, SUD[j * DT + dl].z, red[v]));

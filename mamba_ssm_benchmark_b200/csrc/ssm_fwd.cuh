@@ -234,12 +234,12 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
 #pragma unroll
     for (int i = 0; i < YPL; ++i) {
       const int t = tb + g + i * LPC;
-      float yv = SSM_FWD_LATEZ ? fmaf(Dd0, uu[i], v[i]) : v[i];
-      if (tb >= 0 && dvalid && t < p.L) {
-        if (p.save_ygate) ygout[(long long)t * p.yg.sl] = from_f32<T>(yv);
-        if (p.has_z) yv *= zz[i] * sigmoid(zz[i]);
-        yout[(long long)t * p.y.sl] = from_f32<T>(yv);
-      }
+      const float yv = SSM_FWD_LATEZ ? fmaf(Dd0, uu[i], v[i]) : v[i];
+      // the gate as a select and predicated stores: no branch inside the step loop this runs in
+      const float yo = p.has_z ? yv * (zz[i] * sigmoid(zz[i])) : yv;
+      const bool ok = tb >= 0 && dvalid && t < p.L;
+      if (ok && p.save_ygate) ygout[(long long)t * p.yg.sl] = from_f32<T>(yv);
+      if (ok) yout[(long long)t * p.y.sl] = from_f32<T>(yo);
     }
   };
   // with SSM_FWD_PIPE the previous box's outputs wait here and are emitted from inside the next
