@@ -8,11 +8,14 @@
 // One CTA owns a (batch, 32-channel tile) and walks the sequence backwards in 16-step chunks.
 // For every chunk it
 //   (1) TMA-stages u, delta, z, dy, the saved pre-gate output and B, C;
-//   (2) gate pass, once per (t, d): dys = dy silu(z), dz, dD; and four state-permuted fp32
-//       copies of the B, C tiles (see "state permutation" below);
+//   (2) gate pass, once per (t, d): dys = dy silu(z), dz, dD, the step size (activated when
+//       dt_softplus), packed with u as one float4 per (t, d); and G state-permuted fp32 copies
+//       of the B, C tiles (see "state permutation" below);
 //   (3) recomputes the chunk's 16 states in registers from the checkpoint the forward saved
-//       (chunk_states), caching the decays a_t in shared memory;
-//   (4) runs the reverse adjoint through those registers.
+//       (chunk_states);
+//   (4) runs the reverse adjoint through those registers, recomputing the decays a_t on the MUFU.
+// Both passes fetch step j+-1's inputs while step j computes, and step j's dB|dC reduction is
+// issued after step j-1's arithmetic, so shared-memory and shuffle latency overlap work.
 // No per-step state ever touches HBM.
 //
 // Per element (t, d, n), with dh the total adjoint of h_t (carried + dys_t C_t[n]):

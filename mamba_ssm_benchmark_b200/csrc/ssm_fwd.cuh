@@ -5,10 +5,11 @@
 // (discretize) and :70-76 (the recurrence h_t = a_t h_{t-1} + b_t), y_t = <C_t, h_t>.
 //
 // One warp (= one CTA) owns a (batch, CPW-channel slice, time segment) and walks the segment
-// in boxes of 16 steps that its lane 0 streams through a 4-stage TMA ring: u, delta, z
-// (16 x CPW) and B, C (16 x N).  Every thread keeps its G states in registers; the gated
-// output (and, for training, the pre-gate output) leaves straight from registers.  The state
-// entering every 16-step chunk is written to chunk_states for the backward pass.
+// in 16-step tiles; its lane 0 streams boxes of KB tiles (KB = 2 or 4) through a 2-stage TMA
+// ring: u, delta, z (16 KB x CPW) and B, C (16 KB x N).  Every thread keeps its G states in
+// registers; the gated output (and, for training, the pre-gate output) leaves straight from
+// registers, reduced and stored while the next tile's steps run.  The state entering every
+// 16-step chunk is written to chunk_states for the backward pass.
 //
 // Long sequences with few (batch, channel) tiles are split into S segments: a summary pass
 // (mode kModeSummary) scans every segment from a zero state and records its decay product
