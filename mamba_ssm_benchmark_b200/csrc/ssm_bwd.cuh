@@ -46,6 +46,9 @@
 #ifndef SSM_BWD_PIPE_BC
 #define SSM_BWD_PIPE_BC 1   // reduce step j's dB | dC after step j - 1's math
 #endif
+#ifndef SSM_BWD_PIPE_GATE
+#define SSM_BWD_PIPE_GATE 1   // run chunk i + 1's gate pass inside chunk i's reverse pass
+#endif
 #ifndef SSM_BWD_ACACHE
 // 1: keep the recompute's decays in shared memory for the reverse pass; 0: recompute them on the
 // MUFU (measured faster: config 1 backward 144 us instead of 155 us, the shared-memory pipe being
@@ -60,7 +63,6 @@ struct BwdSmem {
   using Gm = Geo<N, G>;
   static constexpr int TC = Gm::TC, DT = Gm::DT;
   static constexpr int NSTAGE = 2;
-  static constexpr int NOUT = 2;
   static constexpr int ACT = TC * DT * (int)sizeof(T);
   static constexpr int BC = TC * N * (int)sizeof(T);
   static constexpr int OFF_U = 0, OFF_DT = ACT, OFF_Z = 2 * ACT, OFF_DY = 3 * ACT, OFF_YG = 4 * ACT,
@@ -71,22 +73,35 @@ struct BwdSmem {
   static constexpr int OP = PadPitch<Gm::CPW, T>::value;
   static constexpr int OPF = PadPitch<Gm::CPW, float>::value;
   static constexpr int OUT = ((TC * OP * (int)sizeof(T)) + 127) / 128 * 128;
-  // per (t, d) of the chunk, packed for one 128-bit load per step: {u, delta (activated when
-  // dt_softplus), dy silu(z), sigmoid(raw delta + bias) (dt_softplus)}
-  static constexpr int OFF_SUD = NSTAGE * STAGE;
-  static constexpr int OFF_BP = OFF_SUD + TC * DT * 16;        // G perms x (16 x N) fp32 B
-  static constexpr int OFF_CP = OFF_BP + G * TC * N * 4;       // G perms x (16 x N) fp32 C
   // Either the recomputed states (HSMEM) or the decays (ACACHE) are kept in shared memory;
   // the other lives in registers / is recomputed.
   static constexpr bool HSMEM = SSM_BWD_HSMEM != 0 && Gm::NT <= 256;
   static constexpr bool ACACHE = SSM_BWD_ACACHE != 0 && !HSMEM && Gm::NT <= 256;
-  static constexpr int OFF_AC = OFF_CP + G * TC * N * 4;       // decay cache (TC x NT x G) fp32
+  // Gate-pass products of one chunk: per (t, d) {u, delta (activated when dt_softplus), dy silu(z),
+  // sigmoid(raw delta + bias) (dt_softplus)}, packed for one 128-bit load per step, and the G
+  // state-permuted fp32 copies of B and C.
+  static constexpr int SUDB = TC * DT * 16;
+  static constexpr int BPB = G * TC * N * 4;
+  static constexpr int FIXED = NSTAGE * STAGE + ((ACACHE || HSMEM) ? TC * Gm::NT * G * 4 : 0) +
+                               TC * Gm::NW * 2 * N * 4 + Gm::NT * 4 + NSTAGE * 8;
+  // PIPE: chunk i + 1's gate pass runs inside chunk i's reverse pass, so the gate products are
+  // double-buffered and the output tiles triple-buffered; layouts that would not fit keep one
+  // gate buffer and run the gate pass at the top of its own chunk.
+  static constexpr bool PIPE =
+      SSM_BWD_PIPE_GATE != 0 && FIXED + 2 * (SUDB + 2 * BPB) + 3 * 3 * OUT <= 227 * 1024;
+  static constexpr int NBUF = PIPE ? 2 : 1;   // gate-product buffers
+  static constexpr int NOUT = PIPE ? 3 : 2;   // {du, ddelta, dz} output tile sets
+  static constexpr int OFF_SUD = NSTAGE * STAGE;
+  static constexpr int OFF_BP = OFF_SUD + NBUF * SUDB;          // NBUF x G perms x (16 x N) fp32 B
+  static constexpr int OFF_CP = OFF_BP + NBUF * BPB;            // NBUF x G perms x (16 x N) fp32 C
+  static constexpr int OFF_AC = OFF_CP + NBUF * BPB;            // decay cache (TC x NT x G) fp32
   static constexpr int OFF_OUT = OFF_AC + ((ACACHE || HSMEM) ? TC * Gm::NT * G * 4 : 0);   // NOUT x {du, ddelta, dz}
   static constexpr int OFF_RED = OFF_OUT + NOUT * 3 * OUT;     // (TC, NW, 2N) fp32
   static constexpr int OFF_DD = OFF_RED + TC * Gm::NW * 2 * N * 4;   // NT floats (dD partials)
   static constexpr int OFF_BAR = OFF_DD + Gm::NT * 4;
   static constexpr int BYTES = OFF_BAR + NSTAGE * 8;
   static_assert(ACT % 128 == 0 && BC % 128 == 0, "TMA tiles must stay 128-byte aligned");
+  static_assert(BYTES <= 227 * 1024, "backward shared-memory layout exceeds a CTA's limit");
 };
 
 template <typename S>
@@ -222,15 +237,84 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
     }
   }
 
+  // Chunk ci (loop order: ci = 0 is the last chunk of the sequence) lives in stage ci % NSTAGE;
+  // acquire(ci) returns once its input tiles are in shared memory.
+  auto acquire = [&](int ci) {
+    if (p.use_tma) {
+      mbar_wait(&bars[ci % S::NSTAGE], (uint32_t)((ci / S::NSTAGE) & 1), p.err);
+    } else {
+      bwd_coop_load<S, N, NT, T>(p, smem + (ci % S::NSTAGE) * S::STAGE, d0, (nch - 1 - ci) * TC, b);
+      __syncthreads();
+    }
+  };
+  // (2) gate pass over the (t, d) tile of chunk ci: element e = tid + k NT.  Writes the packed
+  // per-(t, d) inputs of the recompute and reverse passes and the dz tile, and adds the element's
+  // d(D) term (counted only when `live`: a pass over a chunk past the end is discarded).
+  constexpr int NE = TC * DT / NT;        // gate elements per thread
+  static_assert((TC * DT) % NT == 0, "the gate pass gives every thread the same number of elements");
+  auto gate_elem = [&](int ci, int k, bool live) {
+    const unsigned char* stg = smem + (ci % S::NSTAGE) * S::STAGE;
+    const T* Xs = reinterpret_cast<const T*>(stg + S::OFF_U);
+    const T* DLs = reinterpret_cast<const T*>(stg + S::OFF_DT);
+    const T* Zs = reinterpret_cast<const T*>(stg + S::OFF_Z);
+    const T* DYs = reinterpret_cast<const T*>(stg + S::OFF_DY);
+    const T* YGs = reinterpret_cast<const T*>(stg + S::OFF_YG);
+    T* DZg = reinterpret_cast<T*>(smem + S::OFF_OUT + (ci % S::NOUT) * 3 * S::OUT + 2 * S::OUT);
+    const int e = tid + k * NT;
+    const int ep = (e / DT) * OP + (e % DT);
+    const float dyv = to_f32(DYs[e]);
+    const float uu = to_f32(Xs[e]);
+    // z terms as selects (without z the Z / YG tiles are stale but finite-or-not values that
+    // are never selected, and the dz tile is not stored)
+    const float zz = to_f32(Zs[e]);
+    const float sg = sigmoid(zz);
+    const float dys = p.has_z ? dyv * zz * sg : dyv;
+    DZg[ep] = from_f32<T>(dyv * to_f32(YGs[e]) * sg * fmaf(zz, 1.0f - sg, 1.0f));
+    dDacc = live ? fmaf(dys, uu, dDacc) : dDacc;   // thread tid always sees channel tid % 32
+    float dtv = to_f32(DLs[e]), sgd = 0.0f;
+    if (p.dt_softplus) {                  // rows past L keep delta = 0 (identity steps)
+      const float xr = dtv + dtb_gate;
+      const bool in = (nch - 1 - ci) * TC + e / DT < p.L;
+      dtv = in ? softplus(xr) : 0.0f;
+      sgd = in ? sigmoid(xr) : 0.0f;
+    }
+    SUD[(ci % S::NBUF) * TC * DT + e] = make_float4(uu, dtv, dys, sgd);
+  };
+  // the state-permuted fp32 copies of chunk ci's B and C: one G-group per thread
+  static_assert(2 * TC * N / G == NT, "every thread permutes one G-group of B or C");
+  auto permute_bc = [&](int ci) {
+    const unsigned char* stg = smem + (ci % S::NSTAGE) * S::STAGE;
+    const int e = tid;
+    const int which = e / (TC * N / G), r = (e % (TC * N / G)) * G;
+    float v[G];
+    loadg<G>(reinterpret_cast<const T*>(stg + (which ? S::OFF_C : S::OFF_B)) + r, v);
+    float* dst = (which ? SCP : SBP) + (ci % S::NBUF) * G * TC * N + r;
+#pragma unroll
+    for (int pm = 0; pm < G; ++pm) {
+      float w[G];
+#pragma unroll
+      for (int j = 0; j < G; ++j) w[j] = v[j ^ pm];
+      storeg<G>(dst + pm * TC * N, w);
+    }
+  };
+  if constexpr (S::PIPE) {                // chunk 0's gate pass; its stage then takes chunk NSTAGE
+    acquire(0);
+#pragma unroll
+    for (int k = 0; k < NE; ++k) gate_elem(0, k, true);
+    permute_bc(0);
+    __syncthreads();
+    if (p.use_tma && tid == 0 && S::NSTAGE < nch)
+      bwd_issue_loads<S>(p, smem, &bars[0], d0, (nch - 1 - S::NSTAGE) * TC, b);
+  }
+
   auto cs_ptr = [&](int ch) { return p.chunk_states + (((size_t)b * nch + ch) * p.D + d) * N + nbase; };
   float2 hs[NP];
   slot_load(cs_ptr(nch - 1), hs);
 
   for (int i = 0; i < nch; ++i) {
     const int ch = nch - 1 - i;
-    const int s = i % S::NSTAGE;
     const int t0 = ch * TC;
-    unsigned char* st = smem + s * S::STAGE;
+    const bool more = i + 1 < nch;        // a next chunk exists (uniform over the CTA)
     float2 hs_next[NP];
     if (ch > 0) {
       slot_load(cs_ptr(ch - 1), hs_next);
@@ -238,67 +322,21 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
 #pragma unroll
       for (int k = 0; k < NP; ++k) hs_next[k] = bc2(0.f);
     }
-
-    if (p.use_tma) {
-      mbar_wait(&bars[s], (uint32_t)((i / S::NSTAGE) & 1), p.err);
-    } else {
-      bwd_coop_load<S, N, NT, T>(p, st, d0, t0, b);
-      __syncthreads();
-    }
-    const T* __restrict__ Xs = reinterpret_cast<const T*>(st + S::OFF_U);
-    const T* __restrict__ DLs = reinterpret_cast<const T*>(st + S::OFF_DT);
     T* DUo = reinterpret_cast<T*>(smem + S::OFF_OUT + (i % S::NOUT) * 3 * S::OUT);
     T* DDTo = reinterpret_cast<T*>(smem + S::OFF_OUT + (i % S::NOUT) * 3 * S::OUT + S::OUT);
     T* DZo = reinterpret_cast<T*>(smem + S::OFF_OUT + (i % S::NOUT) * 3 * S::OUT + 2 * S::OUT);
-
-    // (2) gate pass over (t, d), and the state-permuted fp32 copies of B and C
-    {
-      const T* Zs = reinterpret_cast<const T*>(st + S::OFF_Z);
-      const T* DYs = reinterpret_cast<const T*>(st + S::OFF_DY);
-      const T* YGs = reinterpret_cast<const T*>(st + S::OFF_YG);
-      static_assert((TC * DT) % NT == 0, "the gate pass gives every thread the same number of elements");
+    if constexpr (S::PIPE) {
+      if (more) acquire(i + 1);           // consumed by the gate pass inside this chunk's reverse pass
+    } else {
+      acquire(i);
 #pragma unroll
-      for (int k = 0; k < TC * DT / NT; ++k) {   // a fixed trip count lets the loads be issued together
-        const int e = tid + k * NT;
-        const int ep = (e / DT) * OP + (e % DT);
-        const float dyv = to_f32(DYs[e]);
-        const float uu = to_f32(Xs[e]);
-        float dys = dyv;
-        if (p.has_z) {
-          const float zz = to_f32(Zs[e]);
-          const float sg = sigmoid(zz);
-          dys = dyv * zz * sg;
-          DZo[ep] = from_f32<T>(dyv * to_f32(YGs[e]) * sg * fmaf(zz, 1.0f - sg, 1.0f));
-        }
-        dDacc = fmaf(dys, uu, dDacc);   // thread tid always sees channel tid % 32
-        float dtv = to_f32(DLs[e]), sgd = 0.0f;
-        if (p.dt_softplus) {            // rows past L keep delta = 0 (identity steps)
-          const float xr = dtv + dtb_gate;
-          const bool in = t0 + e / DT < p.L;
-          dtv = in ? softplus(xr) : 0.0f;
-          sgd = in ? sigmoid(xr) : 0.0f;
-        }
-        SUD[e] = make_float4(uu, dtv, dys, sgd);
-      }
-      const T* Bs = reinterpret_cast<const T*>(st + S::OFF_B);
-      const T* Cs = reinterpret_cast<const T*>(st + S::OFF_C);
-      for (int e = tid; e < 2 * TC * N / G; e += NT) {    // one G-group of B or C per iteration
-        const int which = e / (TC * N / G), r = (e % (TC * N / G)) * G;
-        float v[G];
-        loadg<G>((which ? Cs : Bs) + r, v);
-        float* dst = (which ? SCP : SBP) + r;
-#pragma unroll
-        for (int pm = 0; pm < G; ++pm) {
-          float w[G];
-#pragma unroll
-          for (int j = 0; j < G; ++j) w[j] = v[j ^ pm];
-          storeg<G>(dst + pm * TC * N, w);
-        }
-      }
+      for (int k = 0; k < NE; ++k) gate_elem(i, k, true);
+      permute_bc(i);
+      __syncthreads();
     }
-    __syncthreads();
-    const float* __restrict__ Bp = SBP + perm * TC * N + nbase;
-    const float* __restrict__ Cp = SCP + perm * TC * N + nbase;
+    const float4* __restrict__ SUDc = SUD + (i % S::NBUF) * TC * DT;
+    const float* __restrict__ Bp = SBP + (i % S::NBUF) * G * TC * N + perm * TC * N + nbase;
+    const float* __restrict__ Cp = SCP + (i % S::NBUF) * G * TC * N + perm * TC * N + nbase;
     float* __restrict__ Acache = SAC + tid * G;
 
     // (3) recompute the chunk's states from its checkpoint; cache the decays (or the states)
@@ -307,7 +345,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
       float2 hc[NP];
 #pragma unroll
       for (int k = 0; k < NP; ++k) hc[k] = hs[k];
-      float4 rq = SUD[dl];                 // step 0's inputs; each step fetches the next one's
+      float4 rq = SUDc[dl];                 // step 0's inputs; each step fetches the next one's
       float2 rB[NP];
       loadp<G>(Bp, rB);
 #pragma unroll
@@ -317,7 +355,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
 #pragma unroll
         for (int k = 0; k < NP; ++k) Bn[k] = rB[k];
         if (j + 1 < TC) {
-          rq = SUD[(j + 1) * DT + dl];
+          rq = SUDc[(j + 1) * DT + dl];
           loadp<G>(Bp + (j + 1) * N, rB);
         }
         const float uu = q4.x, dtv = q4.y;
@@ -405,7 +443,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
         }
       }
     };
-    float4 qn = SUD[(TC - 1) * DT + dl];   // the last step's inputs, prefetched
+    float4 qn = SUDc[(TC - 1) * DT + dl];   // the last step's inputs, prefetched
     float2 Bnn[NP], Cnn[NP];
     loadp<G>(Bp + (TC - 1) * N, Bnn);
     loadp<G>(Cp + (TC - 1) * N, Cnn);
@@ -424,7 +462,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
           Cn[k] = Cnn[k];
         }
         if (j > 0) {
-          qn = SUD[(j - 1) * DT + dl];
+          qn = SUDc[(j - 1) * DT + dl];
           loadp<G>(Bp + (j - 1) * N, Bnn);
           loadp<G>(Cp + (j - 1) * N, Cnn);
         }
@@ -500,6 +538,14 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
         }
         red[jj * 2 + 0] = -(duN.x + duN.y);
         red[jj * 2 + 1] = ddt.x + ddt.y;
+        if constexpr (S::PIPE) {          // a share of chunk i + 1's gate pass (none past the end)
+          if (jj == 2) {
+            const int q = TC / 4 - 1 - jg;
+#pragma unroll
+            for (int k = q * NE / 4; k < (q + 1) * NE / 4; ++k) gate_elem(i + 1, k, more);
+            if (q == 0) permute_bc(i + 1);
+          }
+        }
         if (S::HSMEM) {
 #pragma unroll
           for (int k = 0; k < NP; ++k) hnext[k] = hprev[k];
@@ -513,12 +559,12 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
           const int j = jg * 4 + (idx >> 1);
           if (idx & 1) {
             // chain rule through softplus(raw + bias), as selects (no branch in the unrolled loop)
-            const float gs = red[v] * SUD[j * DT + dl].w;
+            const float gs = red[v] * SUDc[j * DT + dl].w;
             const float g = p.dt_softplus ? gs : red[v];
             dtbacc += p.dt_softplus ? gs : 0.0f;
             DDTo[j * OP + dl] = from_f32<T>(g);
           } else {
-            DUo[j * OP + dl] = from_f32<T>(fmaf(Dd, SUD[j * DT + dl].z, red[v]));
+            DUo[j * OP + dl] = from_f32<T>(fmaf(Dd, SUDc[j * DT + dl].z, red[v]));
           }
         }
       }
@@ -548,8 +594,11 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
       if (t < p.L) p.part_bc[(((size_t)b * p.ndt + dtile) * p.L + t) * 2 * N + v] = sum;
     }
 
-    if (p.use_tma && tid == 0 && ch - S::NSTAGE >= 0)
-      bwd_issue_loads<S>(p, st, &bars[s], d0, (ch - S::NSTAGE) * TC, b);
+    if (p.use_tma && tid == 0) {          // the stage just consumed takes chunk nx
+      const int nx = (S::PIPE ? i + 1 : i) + S::NSTAGE;
+      if (nx < nch)
+        bwd_issue_loads<S>(p, smem + (nx % S::NSTAGE) * S::STAGE, &bars[nx % S::NSTAGE], d0, (nch - 1 - nx) * TC, b);
+    }
     store_tile<NT, OP>(DUo, p.du, b, t0, d0, p.L, p.D);
     store_tile<NT, OP>(DDTo, p.ddt, b, t0, d0, p.L, p.D);
     if (p.has_z) store_tile<NT, OP>(DZo, p.dz, b, t0, d0, p.L, p.D);
