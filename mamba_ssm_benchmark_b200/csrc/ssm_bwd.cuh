@@ -40,20 +40,15 @@
 
 #include "ssm_common.cuh"
 
-#ifndef SSM_BWD_HSMEM
-#define SSM_BWD_HSMEM 0
-#endif
 #ifndef SSM_BWD_PIPE_BC
 #define SSM_BWD_PIPE_BC 1   // reduce step j's dB | dC after step j - 1's math
 #endif
 #ifndef SSM_BWD_PIPE_GATE
-#define SSM_BWD_PIPE_GATE 1   // run chunk i + 1's gate pass inside chunk i's reverse pass
-#endif
-#ifndef SSM_BWD_ACACHE
-// 1: keep the recompute's decays in shared memory for the reverse pass; 0: recompute them on the
-// MUFU (measured faster: config 1 backward 144 us instead of 155 us, the shared-memory pipe being
-// the busier resource)
-#define SSM_BWD_ACACHE 0
+// 1: chunk i + 1's gate pass runs inside chunk i's reverse pass where the shared-memory budget
+// allows; 0: every gate pass runs at the top of its own chunk.  (Running chunk i + 1's state
+// recompute inside chunk i's reverse pass as well measured slower: 130 us against 124 us for the
+// config-1 backward.)
+#define SSM_BWD_PIPE_GATE 1
 #endif
 
 namespace ssm {
@@ -73,29 +68,25 @@ struct BwdSmem {
   static constexpr int OP = PadPitch<Gm::CPW, T>::value;
   static constexpr int OPF = PadPitch<Gm::CPW, float>::value;
   static constexpr int OUT = ((TC * OP * (int)sizeof(T)) + 127) / 128 * 128;
-  // Either the recomputed states (HSMEM) or the decays (ACACHE) are kept in shared memory;
-  // the other lives in registers / is recomputed.
-  static constexpr bool HSMEM = SSM_BWD_HSMEM != 0 && Gm::NT <= 256;
-  static constexpr bool ACACHE = SSM_BWD_ACACHE != 0 && !HSMEM && Gm::NT <= 256;
   // Gate-pass products of one chunk: per (t, d) {u, delta (activated when dt_softplus), dy silu(z),
   // sigmoid(raw delta + bias) (dt_softplus)}, packed for one 128-bit load per step, and the G
   // state-permuted fp32 copies of B and C.
   static constexpr int SUDB = TC * DT * 16;
   static constexpr int BPB = G * TC * N * 4;
-  static constexpr int FIXED = NSTAGE * STAGE + ((ACACHE || HSMEM) ? TC * Gm::NT * G * 4 : 0) +
-                               TC * Gm::NW * 2 * N * 4 + Gm::NT * 4 + NSTAGE * 8;
-  // PIPE: chunk i + 1's gate pass runs inside chunk i's reverse pass, so the gate products are
-  // double-buffered and the output tiles triple-buffered; layouts that would not fit keep one
-  // gate buffer and run the gate pass at the top of its own chunk.
-  static constexpr bool PIPE =
-      SSM_BWD_PIPE_GATE != 0 && FIXED + 2 * (SUDB + 2 * BPB) + 3 * 3 * OUT <= 227 * 1024;
-  static constexpr int NBUF = PIPE ? 2 : 1;   // gate-product buffers
-  static constexpr int NOUT = PIPE ? 3 : 2;   // {du, ddelta, dz} output tile sets
+  static constexpr int FIXED = NSTAGE * STAGE + TC * Gm::NW * 2 * N * 4 + Gm::NT * 4 + NSTAGE * 8;
+  // bytes with gate products GA chunks ahead: GA + 1 product buffers, GA + 2 output tile sets
+  static constexpr int bytes_for(int ga) { return FIXED + (ga + 1) * (SUDB + 2 * BPB) + (ga + 2) * 3 * OUT; }
+  // per-CTA budget that keeps the CTAs per SM the register file allows (256 threads' worth of
+  // registers at most per 128 threads, G = 2 launches capped at two CTAs per SM)
+  static constexpr int CTAS = (G == 2 || Gm::NT >= 256) ? (G == 2 ? 2 : 1) : 256 / Gm::NT;
+  static constexpr int BUDGET = 228 * 1024 / CTAS - 1024 < 227 * 1024 ? 228 * 1024 / CTAS - 1024 : 227 * 1024;
+  static constexpr int GA = (SSM_BWD_PIPE_GATE >= 1 && bytes_for(1) <= BUDGET) ? 1 : 0;
+  static constexpr int NBUF = GA + 1;          // gate-product buffers
+  static constexpr int NOUT = GA + 2;          // {du, ddelta, dz} output tile sets
   static constexpr int OFF_SUD = NSTAGE * STAGE;
   static constexpr int OFF_BP = OFF_SUD + NBUF * SUDB;          // NBUF x G perms x (16 x N) fp32 B
   static constexpr int OFF_CP = OFF_BP + NBUF * BPB;            // NBUF x G perms x (16 x N) fp32 C
-  static constexpr int OFF_AC = OFF_CP + NBUF * BPB;            // decay cache (TC x NT x G) fp32
-  static constexpr int OFF_OUT = OFF_AC + ((ACACHE || HSMEM) ? TC * Gm::NT * G * 4 : 0);   // NOUT x {du, ddelta, dz}
+  static constexpr int OFF_OUT = OFF_CP + NBUF * BPB;           // NOUT x {du, ddelta, dz}
   static constexpr int OFF_RED = OFF_OUT + NOUT * 3 * OUT;     // (TC, NW, 2N) fp32
   static constexpr int OFF_DD = OFF_RED + TC * Gm::NW * 2 * N * 4;   // NT floats (dD partials)
   static constexpr int OFF_BAR = OFF_DD + Gm::NT * 4;
@@ -156,7 +147,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
   using Gm = Geo<N, G>;
   using S = BwdSmem<N, G, T>;
   constexpr int TC = Gm::TC, DT = Gm::DT, LPC = Gm::LPC, CPW = Gm::CPW, NW = Gm::NW, NT = Gm::NT;
-  constexpr int OP = S::OP, OPF = S::OPF;
+  constexpr int OP = S::OP;
   constexpr int NP = G / 2;                            // state pairs per thread
   constexpr int LC = ilog2(CPW), LG = ilog2(G);
   constexpr int NSLOT = LC < LG ? LC : LG;             // slot-splitting stages (select-free)
@@ -172,7 +163,6 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
   float4* __restrict__ SUD = reinterpret_cast<float4*>(smem + S::OFF_SUD);
   float* __restrict__ SBP = reinterpret_cast<float*>(smem + S::OFF_BP);
   float* __restrict__ SCP = reinterpret_cast<float*>(smem + S::OFF_CP);
-  float* __restrict__ SAC = reinterpret_cast<float*>(smem + S::OFF_AC);
   float* __restrict__ SRED = reinterpret_cast<float*>(smem + S::OFF_RED);
   float* __restrict__ SDD = reinterpret_cast<float*>(smem + S::OFF_DD);
 
@@ -264,8 +254,8 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
     const int ep = (e / DT) * OP + (e % DT);
     const float dyv = to_f32(DYs[e]);
     const float uu = to_f32(Xs[e]);
-    // z terms as selects (without z the Z / YG tiles are stale but finite-or-not values that
-    // are never selected, and the dz tile is not stored)
+    // z terms as selects: without z the Z and YG tiles hold stale values that are never
+    // selected, and the dz tile is not stored
     const float zz = to_f32(Zs[e]);
     const float sg = sigmoid(zz);
     const float dys = p.has_z ? dyv * zz * sg : dyv;
@@ -297,36 +287,98 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
       storeg<G>(dst + pm * TC * N, w);
     }
   };
-  if constexpr (S::PIPE) {                // chunk 0's gate pass; its stage then takes chunk NSTAGE
-    acquire(0);
+  constexpr int GA = S::GA;
+  // Prologue: the gate passes of chunks 0 .. GA-1; their stages then take chunks NSTAGE ..
+  if constexpr (GA > 0) {
 #pragma unroll
-    for (int k = 0; k < NE; ++k) gate_elem(0, k, true);
-    permute_bc(0);
+    for (int c0 = 0; c0 < GA; ++c0) {
+      if (c0 < nch) {
+        acquire(c0);
+#pragma unroll
+        for (int k = 0; k < NE; ++k) gate_elem(c0, k, true);
+        permute_bc(c0);
+      }
+    }
     __syncthreads();
-    if (p.use_tma && tid == 0 && S::NSTAGE < nch)
-      bwd_issue_loads<S>(p, smem, &bars[0], d0, (nch - 1 - S::NSTAGE) * TC, b);
+    if (p.use_tma && tid == 0) {
+      for (int c0 = S::NSTAGE; c0 < S::NSTAGE + GA && c0 < nch; ++c0)
+        bwd_issue_loads<S>(p, smem + (c0 % S::NSTAGE) * S::STAGE, &bars[c0 % S::NSTAGE], d0, (nch - 1 - c0) * TC, b);
+    }
   }
 
+  // (3) one recompute step: hc advances by step r of the chunk whose gate products are at
+  // (sud, bp); rq / rB hold step r's inputs (fetched one step ahead) and are refilled with step
+  // r + 1's
+  auto rec_step = [&](float2 (&hc)[NP], float4& rq, float2 (&rB)[NP], const float4* sud, const float* bp, int r) {
+    const float4 q4 = rq;
+    float2 Bn[NP];
+#pragma unroll
+    for (int k = 0; k < NP; ++k) Bn[k] = rB[k];
+    if (r + 1 < TC) {
+      rq = sud[(r + 1) * DT + dl];
+      loadp<G>(bp + (r + 1) * N, rB);
+    }
+    const float uu = q4.x, dtv = q4.y;
+    const float2 u2 = bc2(uu), dt2 = bc2(dtv), dtu2 = bc2(dtv * uu);
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+      if (METHOD == kZOH) {
+        const float2 a = ex2x2(mul2(dt2, A2[k]));
+        const float2 ng = mul2(mul2(Bn[k], u2), niA[k]);
+        hc[k] = fma2(a, fma2(ng, bc2(-1.0f), hc[k]), ng);
+      } else if (METHOD == kEuler) {
+        const float2 a = ex2x2(mul2(dt2, A2[k]));
+        hc[k] = fma2(a, hc[k], mul2(dtu2, Bn[k]));
+      } else {
+        const float2 zz = mul2(dt2, Ak[k]);
+        const float2 w = rcpx2(fma2(bc2(-0.5f), zz, bc2(1.0f)));
+        hc[k] = fma2(mul2(fma2(bc2(0.5f), zz, bc2(1.0f)), w), hc[k], mul2(mul2(dtu2, Bn[k]), w));
+      }
+    }
+  };
+  auto sud_buf = [&](int ci) { return SUD + (ci % S::NBUF) * TC * DT; };
+  auto bp_buf = [&](int ci) { return SBP + (ci % S::NBUF) * G * TC * N + perm * TC * N + nbase; };
+  // the chunk's states, step by step, from the state entering it
+  float2 H[TC][NP];
+  auto rec_chunk = [&](const float2 (&h_in)[NP], int ci) {
+    float2 hc[NP];
+#pragma unroll
+    for (int k = 0; k < NP; ++k) hc[k] = h_in[k];
+    const float4* sud = sud_buf(ci);
+    const float* bp = bp_buf(ci);
+    float4 rq = sud[dl];                  // step 0's inputs
+    float2 rB[NP];
+    loadp<G>(bp, rB);
+#pragma unroll
+    for (int j = 0; j < TC; ++j) {
+      rec_step(hc, rq, rB, sud, bp, j);
+#pragma unroll
+      for (int k = 0; k < NP; ++k) H[j][k] = hc[k];
+    }
+  };
+
   auto cs_ptr = [&](int ch) { return p.chunk_states + (((size_t)b * nch + ch) * p.D + d) * N + nbase; };
-  float2 hs[NP];
-  slot_load(cs_ptr(nch - 1), hs);
+  auto cs_load = [&](int ch, float2 (&o)[NP]) {   // the state entering chunk ch (zero before chunk 0)
+    if (ch >= 0) {
+      slot_load(cs_ptr(ch), o);
+    } else {
+#pragma unroll
+      for (int k = 0; k < NP; ++k) o[k] = bc2(0.f);
+    }
+  };
+  float2 hs[NP];                          // the state entering chunk i
+  cs_load(nch - 1, hs);
 
   for (int i = 0; i < nch; ++i) {
     const int ch = nch - 1 - i;
     const int t0 = ch * TC;
-    const bool more = i + 1 < nch;        // a next chunk exists (uniform over the CTA)
-    float2 hs_next[NP];
-    if (ch > 0) {
-      slot_load(cs_ptr(ch - 1), hs_next);
-    } else {
-#pragma unroll
-      for (int k = 0; k < NP; ++k) hs_next[k] = bc2(0.f);
-    }
+    float2 hs_next[NP];                   // the state entering chunk i + 1
+    cs_load(ch - 1, hs_next);
     T* DUo = reinterpret_cast<T*>(smem + S::OFF_OUT + (i % S::NOUT) * 3 * S::OUT);
     T* DDTo = reinterpret_cast<T*>(smem + S::OFF_OUT + (i % S::NOUT) * 3 * S::OUT + S::OUT);
     T* DZo = reinterpret_cast<T*>(smem + S::OFF_OUT + (i % S::NOUT) * 3 * S::OUT + 2 * S::OUT);
-    if constexpr (S::PIPE) {
-      if (more) acquire(i + 1);           // consumed by the gate pass inside this chunk's reverse pass
+    if constexpr (GA > 0) {
+      if (i + GA < nch) acquire(i + GA);  // consumed by the gate pass inside this chunk's reverse pass
     } else {
       acquire(i);
 #pragma unroll
@@ -334,60 +386,13 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
       permute_bc(i);
       __syncthreads();
     }
-    const float4* __restrict__ SUDc = SUD + (i % S::NBUF) * TC * DT;
-    const float* __restrict__ Bp = SBP + (i % S::NBUF) * G * TC * N + perm * TC * N + nbase;
+    const float4* __restrict__ SUDc = sud_buf(i);
+    const float* __restrict__ Bp = bp_buf(i);
     const float* __restrict__ Cp = SCP + (i % S::NBUF) * G * TC * N + perm * TC * N + nbase;
-    float* __restrict__ Acache = SAC + tid * G;
-
-    // (3) recompute the chunk's states from its checkpoint; cache the decays (or the states)
-    float2 H[S::HSMEM ? 1 : TC][NP];
-    {
-      float2 hc[NP];
-#pragma unroll
-      for (int k = 0; k < NP; ++k) hc[k] = hs[k];
-      float4 rq = SUDc[dl];                 // step 0's inputs; each step fetches the next one's
-      float2 rB[NP];
-      loadp<G>(Bp, rB);
-#pragma unroll
-      for (int j = 0; j < TC; ++j) {
-        const float4 q4 = rq;
-        float2 Bn[NP], av[NP];
-#pragma unroll
-        for (int k = 0; k < NP; ++k) Bn[k] = rB[k];
-        if (j + 1 < TC) {
-          rq = SUDc[(j + 1) * DT + dl];
-          loadp<G>(Bp + (j + 1) * N, rB);
-        }
-        const float uu = q4.x, dtv = q4.y;
-        const float2 u2 = bc2(uu), dt2 = bc2(dtv), dtu2 = bc2(dtv * uu);
-#pragma unroll
-        for (int k = 0; k < NP; ++k) {
-          if (METHOD == kZOH) {
-            const float2 a = ex2x2(mul2(dt2, A2[k]));
-            const float2 ng = mul2(mul2(Bn[k], u2), niA[k]);
-            hc[k] = fma2(a, fma2(ng, bc2(-1.0f), hc[k]), ng);
-            av[k] = a;
-          } else if (METHOD == kEuler) {
-            const float2 a = ex2x2(mul2(dt2, A2[k]));
-            hc[k] = fma2(a, hc[k], mul2(dtu2, Bn[k]));
-            av[k] = a;
-          } else {
-            const float2 zz = mul2(dt2, Ak[k]);
-            const float2 w = rcpx2(fma2(bc2(-0.5f), zz, bc2(1.0f)));
-            hc[k] = fma2(mul2(fma2(bc2(0.5f), zz, bc2(1.0f)), w), hc[k], mul2(mul2(dtu2, Bn[k]), w));
-            av[k] = w;   // bilinear caches w = 1/(1 - z/2); a = (1 + z/2) w
-          }
-          if (!S::HSMEM) H[S::HSMEM ? 0 : j][k] = hc[k];
-        }
-        if (S::ACACHE) storep<G>(Acache + j * NT * G, av);
-        if (S::HSMEM) storep<G>(Acache + j * NT * G, hc);
-      }
-    }
+    rec_chunk(hs, i);
 
     // (4) reverse adjoint through the chunk.  du and dB are accumulated negated (-du, -dB),
     // which turns every per-state update into one packed FMA.
-    float2 hnext[NP];            // HSMEM: state of step j, carried from step j + 1's load
-    if (S::HSMEM) loadp<G>(Acache + (TC - 1) * NT * G, hnext);
     float2 pend_b[NP], pend_c[NP];        // SSM_BWD_PIPE_BC: the previous step's dB | dC values
     // dB | dC of step js over the warp's channels: slot-splitting stages first (a fixed register
     // slot is sent on every lane thanks to the state permutation), then one stage that splits
@@ -455,7 +460,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
         const int j = jg * 4 + jj;
         // step j's inputs were fetched one step ahead; fetch step j - 1's now
         const float4 q4 = qn;
-        float2 Bn[NP], Cn[NP], av[NP], hprev[NP];
+        float2 Bn[NP], Cn[NP], av[NP];
 #pragma unroll
         for (int k = 0; k < NP; ++k) {
           Bn[k] = Bnn[k];
@@ -468,28 +473,16 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
         }
         const float uu = q4.x, dtv = q4.y, dys = q4.z;
         const float2 u2 = bc2(uu), dt2 = bc2(dtv), dys2 = bc2(dys);
-        if (S::ACACHE) {
-          loadp<G>(Acache + j * NT * G, av);
-        } else {
 #pragma unroll
-          for (int k = 0; k < NP; ++k)
-            av[k] = (METHOD == kBilinear) ? rcpx2(fma2(mul2(bc2(-0.5f), dt2), Ak[k], bc2(1.0f)))
-                                          : ex2x2(mul2(dt2, A2[k]));
-        }
-        if (S::HSMEM) {
-          if (j > 0) {
-            loadp<G>(Acache + (j > 0 ? j - 1 : 0) * NT * G, hprev);
-          } else {
-#pragma unroll
-            for (int k = 0; k < NP; ++k) hprev[k] = hs[k];
-          }
-        }
+        for (int k = 0; k < NP; ++k)
+          av[k] = (METHOD == kBilinear) ? rcpx2(fma2(mul2(bc2(-0.5f), dt2), Ak[k], bc2(1.0f)))
+                                        : ex2x2(mul2(dt2, A2[k]));
         float2 duN = bc2(0.f), ddt = bc2(0.f);
         float2 bBN[NP], bC[NP];
 #pragma unroll
         for (int k = 0; k < NP; ++k) {
-          const float2 ht = S::HSMEM ? hnext[k] : H[S::HSMEM ? 0 : j][k];
-          const float2 hp = S::HSMEM ? hprev[k] : ((j > 0) ? H[(S::HSMEM || j == 0) ? 0 : j - 1][k] : hs[k]);
+          const float2 ht = H[j][k];
+          const float2 hp = (j > 0) ? H[j > 0 ? j - 1 : 0][k] : hs[k];
           const float2 Bu = mul2(Bn[k], u2);
           dh[k] = fma2(dys2, Cn[k], dh[k]);
           bC[k] = mul2(dys2, ht);
@@ -538,17 +531,13 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
         }
         red[jj * 2 + 0] = -(duN.x + duN.y);
         red[jj * 2 + 1] = ddt.x + ddt.y;
-        if constexpr (S::PIPE) {          // a share of chunk i + 1's gate pass (none past the end)
+        if constexpr (GA > 0) {           // a share of chunk i + GA's gate pass (none past the end)
           if (jj == 2) {
             const int q = TC / 4 - 1 - jg;
 #pragma unroll
-            for (int k = q * NE / 4; k < (q + 1) * NE / 4; ++k) gate_elem(i + 1, k, more);
-            if (q == 0) permute_bc(i + 1);
+            for (int k = q * NE / 4; k < (q + 1) * NE / 4; ++k) gate_elem(i + GA, k, i + GA < nch);
+            if (q == 0) permute_bc(i + GA);
           }
-        }
-        if (S::HSMEM) {
-#pragma unroll
-          for (int k = 0; k < NP; ++k) hnext[k] = hprev[k];
         }
       }
       xpose_reduce<QV, LPC, 1>(red, lane);
@@ -595,7 +584,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
     }
 
     if (p.use_tma && tid == 0) {          // the stage just consumed takes chunk nx
-      const int nx = (S::PIPE ? i + 1 : i) + S::NSTAGE;
+      const int nx = i + GA + S::NSTAGE;
       if (nx < nch)
         bwd_issue_loads<S>(p, smem + (nx % S::NSTAGE) * S::STAGE, &bars[nx % S::NSTAGE], d0, (nch - 1 - nx) * TC, b);
     }
