@@ -196,7 +196,10 @@ def e2e_run(cfg, device, steps, world, seed):
     """Public API with host buffers: every step copies its inputs from pinned host memory, runs the
     forward and backward through selective_scan_fused + autograd, and copies every output back to
     pinned host memory.  The copies run on their own streams with double-buffered device inputs, so
-    step i's device-to-host copy and step i+1's host-to-device copy overlap step i's compute."""
+    step i's device-to-host copy and step i+1's host-to-device copy overlap step i's compute.
+    A step's outputs are held until the step two later, whose compute first waits for their
+    device-to-host copy, so the allocator reuses their blocks in stream order (recording them
+    on the copy stream instead kept the allocator growing with fresh device allocations)."""
     from mamba_ssm_benchmark_b200 import selective_scan_fused, sharding
     from mamba_ssm_benchmark_b200.workloads import make_inputs
     ins = make_inputs(cfg.B, cfg.L, cfg.D, cfg.N, seed=seed, dist="config", dtype=cfg.dtype)
@@ -207,6 +210,8 @@ def e2e_run(cfg, device, steps, world, seed):
     dev_sets = [{k: torch.empty(v.shape, dtype=v.dtype, device=device) for k, v in host.items()} for _ in range(2)]
     up_done = [torch.cuda.Event() for _ in range(2)]
     comp_done = [torch.cuda.Event() for _ in range(2)]
+    down_done = [torch.cuda.Event() for _ in range(2)]
+    held = [None, None]                           # outputs whose device-to-host copies may still run
     outs_host = [None, None]
     d2h = 0
 
@@ -220,6 +225,8 @@ def e2e_run(cfg, device, steps, world, seed):
     def compute_step(k):
         nonlocal d2h
         compute.wait_event(up_done[k])
+        compute.wait_event(down_done[k])          # slot k's previous outputs are copied out ...
+        held[k] = None                            # ... so this step may reuse their blocks
         dv = dev_sets[k]
         leaves = [dv[n].detach().requires_grad_() for n in ("u", "delta", "A", "Bm", "Cm", "Dskip", "z")]
         y, last = selective_scan_fused(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4], D=leaves[5],
@@ -235,7 +242,8 @@ def e2e_run(cfg, device, steps, world, seed):
         with torch.cuda.stream(down):
             for o, r in zip(outs_host[k], res):
                 o.copy_(r, non_blocking=True)
-                r.record_stream(down)
+        down_done[k].record(down)
+        held[k] = res
         d2h = sum(r.numel() * r.element_size() for r in res)
 
     def run(n):
@@ -263,6 +271,47 @@ def e2e_run(cfg, device, steps, world, seed):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = t.item()
     return ms / steps, h2d, d2h
+
+
+def host_link(device, h2d, d2h, tokens_step, e2e_value, world, reps=8):
+    """The host link's floor for the e2e step: device time to copy h2d bytes from pinned host
+    memory to the device and d2h bytes back at the same time (one copy each way per repetition,
+    on two streams), max over ranks.  Returns the e2e "link" record: that time, the bandwidth,
+    the tokens/s the copies alone would allow and the e2e value's fraction of it."""
+    hu = torch.empty(h2d, dtype=torch.uint8).pin_memory()
+    du = torch.empty(h2d, dtype=torch.uint8, device=device)
+    hd = torch.empty(d2h, dtype=torch.uint8).pin_memory()
+    dd = torch.zeros(d2h, dtype=torch.uint8, device=device)
+    cur = torch.cuda.current_stream(device)
+    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+
+    def burst(n):
+        up.wait_stream(cur)
+        down.wait_stream(cur)
+        for _ in range(n):
+            with torch.cuda.stream(up):
+                du.copy_(hu, non_blocking=True)
+            with torch.cuda.stream(down):
+                hd.copy_(dd, non_blocking=True)
+        cur.wait_stream(up)
+        cur.wait_stream(down)
+
+    burst(2)
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    burst(reps)
+    e1.record(cur)
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / reps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+    bound = tokens_step / (ms / 1e3)
+    return {"ms_per_step": ms, "gbs": (h2d + d2h) / (ms / 1e3) / 1e9, "bound_value": bound,
+            "frac": e2e_value / bound,
+            "what": "pinned H2D of the step's input bytes and D2H of its output bytes, at the same time"}
 
 
 def cpu_reference_sample(cfg, budget_s, d_slice=None, b_rows=None, repeats_min=3, backward=True):
@@ -682,6 +731,7 @@ def main():
 
     e2e_ms, h2d, d2h = e2e_run(cfg, device, args.e2e_steps, world, seed=77 + rank)
     e2e_value = tokens_step / (e2e_ms / 1e3)
+    link = host_link(device, h2d, d2h, tokens_step, e2e_value, world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -709,7 +759,7 @@ def main():
                          "algorithmic_bytes_per_launch": bwd_bytes, "avg_launch_ms": bwd_ms,
                          "mufu": mufu_bound(cfg, bwd_ms, clk)},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": args.e2e_steps},
+                    "steps": args.e2e_steps, "link": link},
             "gpu_launches": K * steps[0].launches,
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
                        "samples": clk["samples"]},
