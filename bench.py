@@ -314,6 +314,18 @@ def host_link(device, h2d, d2h, tokens_step, e2e_value, world, reps=8):
             "what": "pinned H2D of the step's input bytes and D2H of its output bytes, at the same time"}
 
 
+def cpu_model():
+    """The host CPU's model name (from /proc/cpuinfo), for the CPU baseline records."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for row in f:
+                if row.startswith("model name"):
+                    return row.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_reference_sample(cfg, budget_s, d_slice=None, b_rows=None, repeats_min=3, backward=True):
     """Oracle port (the reference's chunked CPU scan + recomputing backward) on a slice of the
     workload; returns (tokens/s in 512-channel token units, description, samples)."""
@@ -387,7 +399,8 @@ def run_reference(args, cfg, workload):
             "higher_is_better": True, "scaling": "strong" if args.config == 2 else "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
             "config": {"workload": workload, "B": cfg.B, "L": cfg.L, "D": cfg.D, "N": cfg.N},
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "cpu_model": cpu_model(),
+                             "kind": "port",
                              "sample": sample + "; oracle/scan_oracle.py restates models/scan.py (chunked)"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -513,7 +526,8 @@ def run_sequence_shards(args, cfg, workload, rank, world, device):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, desc, _ = cpu_reference_sample(cfg, budget_s=12.0, b_rows=1, d_slice=16, backward=False)
-        cpu = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+        cpu = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(), "cpu_model": cpu_model(),
+               "kind": "port",
                "sample": desc + "; tokens counted in 512-channel units; oracle/scan_oracle.py restates "
                                 "models/scan.py (chunked scan)"}
     if rank == 0:
@@ -737,7 +751,8 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, desc, _ = cpu_reference_sample(cfg, budget_s=12.0, b_rows=max(1, cfg.B // 8) if cfg.B > 1 else 1,
                                              d_slice=cfg.D if args.config == 1 else 128)
-        cpu = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+        cpu = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(), "cpu_model": cpu_model(),
+               "kind": "port",
                "sample": desc + "; oracle/scan_oracle.py restates models/scan.py (chunked scan)"}
 
     if rank == 0:
