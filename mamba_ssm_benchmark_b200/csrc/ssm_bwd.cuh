@@ -40,17 +40,6 @@
 
 #include "ssm_common.cuh"
 
-#ifndef SSM_BWD_PIPE_BC
-#define SSM_BWD_PIPE_BC 1   // reduce step j's dB | dC after step j - 1's math
-#endif
-#ifndef SSM_BWD_PIPE_GATE
-// 1: chunk i + 1's gate pass runs inside chunk i's reverse pass where the shared-memory budget
-// allows; 0: every gate pass runs at the top of its own chunk.  (Running chunk i + 1's state
-// recompute inside chunk i's reverse pass as well measured slower: 130 us against 124 us for the
-// config-1 backward.)
-#define SSM_BWD_PIPE_GATE 1
-#endif
-
 namespace ssm {
 
 template <int N, int G, typename T>
@@ -80,7 +69,12 @@ struct BwdSmem {
   // registers at most per 128 threads, G = 2 launches capped at two CTAs per SM)
   static constexpr int CTAS = (G == 2 || Gm::NT >= 256) ? (G == 2 ? 2 : 1) : 256 / Gm::NT;
   static constexpr int BUDGET = 228 * 1024 / CTAS - 1024 < 227 * 1024 ? 228 * 1024 / CTAS - 1024 : 227 * 1024;
-  static constexpr int GA = (SSM_BWD_PIPE_GATE >= 1 && bytes_for(1) <= BUDGET) ? 1 : 0;
+  // GA = 1: chunk i + 1's gate pass runs inside chunk i's reverse pass, so the gate products are
+  // double-buffered and the output tiles triple-buffered; layouts that would lose a CTA per SM
+  // that way keep one gate buffer (GA = 0) and run the gate pass at the top of its own chunk.
+  // (Running chunk i + 1's state recompute inside chunk i's reverse pass as well, with the gate
+  // two chunks ahead, measured slower: 130 us against 124 us for the config-1 backward.)
+  static constexpr int GA = bytes_for(1) <= BUDGET ? 1 : 0;
   static constexpr int NBUF = GA + 1;          // gate-product buffers
   static constexpr int NOUT = GA + 2;          // {du, ddelta, dz} output tile sets
   static constexpr int OFF_SUD = NSTAGE * STAGE;
@@ -393,11 +387,11 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
 
     // (4) reverse adjoint through the chunk.  du and dB are accumulated negated (-du, -dB),
     // which turns every per-state update into one packed FMA.
-    float2 pend_b[NP], pend_c[NP];        // SSM_BWD_PIPE_BC: the previous step's dB | dC values
+    float2 pend_b[NP], pend_c[NP];        // the previous step's dB | dC values
     // dB | dC of step js over the warp's channels: slot-splitting stages first (a fixed register
     // slot is sent on every lane thanks to the state permutation), then one stage that splits
-    // dB from dC, then all-reduce stages for the remaining channel bits.  With SSM_BWD_PIPE_BC
-    // step j's reduction runs after step j - 1's math, so its shuffle latency overlaps work.
+    // dB from dC, then all-reduce stages for the remaining channel bits.  Step j's reduction runs
+    // after step j - 1's math, so its shuffle latency overlaps work.
     auto reduce_bc = [&](float2 (&xb)[NP], float2 (&xc)[NP], int js) {
       if constexpr (G == 4 && LC >= 1) {   // slot bit 1: keep pair 0, receive the partner's pair 1
         constexpr int m = (CPW / 2) * LPC;
@@ -519,15 +513,13 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
             dh[k] = mul2(dh[k], a);
           }
         }
-        if (SSM_BWD_PIPE_BC) {
-          if (j < TC - 1) reduce_bc(pend_b, pend_c, j + 1);
+        // step j + 1's dB | dC reduction after step j's math (config-1 backward 124 us, against
+        // 130 us when step j is reduced here)
+        if (j < TC - 1) reduce_bc(pend_b, pend_c, j + 1);
 #pragma unroll
-          for (int k = 0; k < NP; ++k) {
-            pend_b[k] = bBN[k];
-            pend_c[k] = bC[k];
-          }
-        } else {
-          reduce_bc(bBN, bC, j);
+        for (int k = 0; k < NP; ++k) {
+          pend_b[k] = bBN[k];
+          pend_c[k] = bC[k];
         }
         red[jj * 2 + 0] = -(duN.x + duN.y);
         red[jj * 2 + 1] = ddt.x + ddt.y;
@@ -559,15 +551,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
       }
     }
 
-    if (SSM_BWD_PIPE_BC) {               // step 0's dB | dC
-      float2 nb[NP], nc[NP];
-#pragma unroll
-      for (int k = 0; k < NP; ++k) {
-        nb[k] = pend_b[k];
-        nc[k] = pend_c[k];
-      }
-      reduce_bc(nb, nc, 0);
-    }
+    reduce_bc(pend_b, pend_c, 0);         // step 0's dB | dC
     __syncthreads();
 
     // cross-warp dB | dC sum -> this CTA's partial (fixed order); TC * 2N = G * NT elements

@@ -59,12 +59,6 @@ struct FwdSmem {
 // h' = a (h + g) - g with g = B u / A; the coefficient kept is ng = -g (so both uses are one
 // packed FMA): h + g = fma(ng, -1, h), h' = fma(a, h + g, ng).  Euler and bilinear use
 // h' = a h + b.
-#ifndef SSM_CHAIN1
-// 1: the forward's ZOH recurrence runs as h' = a h + b with b = g (1 - a), g = -B u / A, formed in
-// phase A (one FMA per step on the dependency chain); 0: h' = a (h - g) + g in phase B (two).
-// (The backward's recompute keeps the second form: measured faster there.)
-#define SSM_CHAIN1 1
-#endif
 
 template <int METHOD>
 __device__ __forceinline__ void fwd_coeffs2(float2 dt2, float2 u2, float2 dtu2, float2 B2, float2 Ak2, float2 A2k2,
@@ -72,7 +66,7 @@ __device__ __forceinline__ void fwd_coeffs2(float2 dt2, float2 u2, float2 dtu2, 
   if (METHOD == kZOH) {
     a = ex2x2(mul2(dt2, A2k2));
     bco = mul2(mul2(B2, u2), niA2);
-    if (SSM_CHAIN1) bco = fma2(bco, make_float2(-a.x, -a.y), bco);
+    bco = fma2(bco, make_float2(-a.x, -a.y), bco);   // b = g (1 - a): one FMA per step on the chain
   } else if (METHOD == kEuler) {
     a = ex2x2(mul2(dt2, A2k2));
     bco = mul2(dtu2, B2);
@@ -85,25 +79,10 @@ __device__ __forceinline__ void fwd_coeffs2(float2 dt2, float2 u2, float2 dtu2, 
 }
 template <int METHOD>
 __device__ __forceinline__ float2 fwd_apply2(float2 h, float2 a, float2 bco) {
-  if (METHOD == kZOH && !SSM_CHAIN1) return fma2(a, fma2(bco, bc2(-1.0f), h), bco);
   return fma2(a, h, bco);
 }
 
-#ifndef SSM_FWD_SUB
-#define SSM_FWD_SUB 4   // steps per state-independent sub-tile (divides 16)
-#endif
-#ifndef SSM_FWD_PIPE
-#define SSM_FWD_PIPE 1   // reduce and store box i's outputs while box i + 1's steps run
-#endif
-#ifndef SSM_FWD_PREF
-#define SSM_FWD_PREF 1   // fetch sub-tile k + 1's inputs before computing sub-tile k
-#endif
-#ifndef SSM_FWD_LATEZ
-#define SSM_FWD_LATEZ 1   // z and the D-skip input are read for the lane's output steps only, at the box end
-#endif
-#ifndef SSM_FWD_GMAJOR
-#define SSM_FWD_GMAJOR 1   // lane = g * CPW + c (state group major) instead of c * LPC + g
-#endif
+constexpr int kFwdSub = 4;   // steps per state-independent sub-tile of the forward (divides 16)
 
 template <typename S, int MODE>
 __device__ __forceinline__ void fwd_issue_loads(const FwdParams& p, unsigned char* st, uint64_t* bar, int x0,
@@ -163,8 +142,8 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
   // so the vector loads of B and C read one address per quarter warp (a broadcast) instead of
   // LPC different ones.
   const int lane = threadIdx.x;
-  const int c = SSM_FWD_GMAJOR ? lane % CPW : lane / LPC, g = SSM_FWD_GMAJOR ? lane / CPW : lane % LPC;
-  constexpr int GSTRIDE = SSM_FWD_GMAJOR ? CPW : 1;   // lane distance between a channel's state groups
+  const int c = lane % CPW, g = lane / CPW;
+  constexpr int GSTRIDE = CPW;   // lane distance between a channel's state groups
   const int b = blockIdx.z, seg = blockIdx.y;
   const int d0 = blockIdx.x * CPW;
   const int x0 = (d0 / BXC) * BXC, dl = d0 - x0 + c;   // box origin and this lane's column
@@ -194,8 +173,8 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
       niA[i] = make_float2(-1.0f / av[2 * i], -1.0f / av[2 * i + 1]);
     }
   }
-  // D skip folded into the partial sum of lane g == 0 of each channel group
-  const float Dd0 = (MODE == kModeMain && p.Dskip != nullptr && dvalid && (SSM_FWD_LATEZ || g == 0)) ? p.Dskip[d] : 0.0f;
+  // D skip, added to the reduced y of the lane's output steps
+  const float Dd0 = (MODE == kModeMain && p.Dskip != nullptr && dvalid) ? p.Dskip[d] : 0.0f;
 
   float2 h[NP], P[NP];
 #pragma unroll
@@ -235,7 +214,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
 #pragma unroll
     for (int i = 0; i < YPL; ++i) {
       const int t = tb + g + i * LPC;
-      const float yv = SSM_FWD_LATEZ ? fmaf(Dd0, uu[i], v[i]) : v[i];
+      const float yv = fmaf(Dd0, uu[i], v[i]);
       // the gate as a select and predicated stores: no branch inside the step loop this runs in
       const float yo = p.has_z ? yv * (zz[i] * sigmoid(zz[i])) : yv;
       const bool ok = tb >= 0 && dvalid && t < p.L;
@@ -243,8 +222,8 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
       if (ok) yout[(long long)t * p.y.sl] = from_f32<T>(yo);
     }
   };
-  // with SSM_FWD_PIPE the previous box's outputs wait here and are emitted from inside the next
-  // box's step loop, so their shuffles, MUFU work and stores overlap the recurrence
+  // the previous tile's outputs wait here and are emitted from inside the next tile's step loop,
+  // so their shuffles, MUFU work and stores overlap the recurrence
   float ypv[TC], zpv[TC / LPC], upv[TC / LPC];
   int tpv = -1;
 #pragma unroll
@@ -308,10 +287,10 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
     if constexpr (MODE == kModeAdjoint) {
       // reverse through the box: dh <- a_t dh + a_t C_t dys_t, dys = dy silu(z) (or dy)
 #pragma unroll
-      for (int t0s = TC - SSM_FWD_SUB; t0s >= 0; t0s -= SSM_FWD_SUB) {
-        float2 av[SSM_FWD_SUB][NP], cd[SSM_FWD_SUB][NP];
+      for (int t0s = TC - kFwdSub; t0s >= 0; t0s -= kFwdSub) {
+        float2 av[kFwdSub][NP], cd[kFwdSub][NP];
 #pragma unroll
-        for (int q = 0; q < SSM_FWD_SUB; ++q) {
+        for (int q = 0; q < kFwdSub; ++q) {
           const int tt = t0s + q;
           float dys = to_f32(Xs[tt * BXC + dl]);
           const float dtv = delta_at(tt * BXC + dl);
@@ -330,7 +309,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
           }
         }
 #pragma unroll
-        for (int q = SSM_FWD_SUB - 1; q >= 0; --q) {
+        for (int q = kFwdSub - 1; q >= 0; --q) {
 #pragma unroll
           for (int i = 0; i < NP; ++i) {
             h[i] = fma2(av[q][i], h[i], cd[q][i]);
@@ -339,18 +318,18 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
         }
       }
     } else {
-      // 16 steps.  The lane's partial y (its G states, plus D u on lane 0 of the group) stays
-      // in registers, stored at yp[(t % LPC) YPL + t / LPC] so that after the reduction lane g
-      // holds steps g, g + LPC, ...; the lane also keeps z of those steps.  Steps are processed
-      // in sub-tiles: phase A computes what does not depend on the state (decays, inputs, C),
-      // phase B is only the recurrence and the y accumulation.
-      // the sub-tile's inputs from shared memory; with SSM_FWD_PREF the next sub-tile's are fetched
-      // before this one's coefficients are computed, so the loads' latency overlaps the work
-      float fu[2][SSM_FWD_SUB], fdt[2][SSM_FWD_SUB];
-      float2 fB[2][SSM_FWD_SUB][NP], fC[2][SSM_FWD_SUB][NP];
+      // 16 steps.  The lane's partial y (over its G states) stays in registers, stored at
+      // yp[(t % LPC) YPL + t / LPC] so that after the reduction lane g holds steps g, g + LPC, ...;
+      // the lane also keeps z and u of those steps (read after the step loop).  Steps are
+      // processed in sub-tiles: phase A computes what does not depend on the state (decays,
+      // inputs, C), phase B is only the recurrence and the y accumulation.  The next sub-tile's
+      // inputs are fetched from shared memory before this one's coefficients are computed, so the
+      // loads' latency overlaps the work.
+      float fu[2][kFwdSub], fdt[2][kFwdSub];
+      float2 fB[2][kFwdSub][NP], fC[2][kFwdSub][NP];
       auto fetch = [&](int slot, int base) {
 #pragma unroll
-        for (int q = 0; q < SSM_FWD_SUB; ++q) {
+        for (int q = 0; q < kFwdSub; ++q) {
           const int tt = base + q;
           fu[slot][q] = to_f32(Xs[tt * BXC + dl]);
           fdt[slot][q] = delta_at(tt * BXC + dl);
@@ -358,17 +337,14 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
           if (MODE == kModeMain) loadp<G>(Cs + tt * N + nbase, fC[slot][q]);
         }
       };
-      if (SSM_FWD_PREF) fetch(0, 0);
+      fetch(0, 0);
 #pragma unroll
-      for (int t0s = 0; t0s < TC; t0s += SSM_FWD_SUB) {
-        const int cur = SSM_FWD_PREF ? (t0s / SSM_FWD_SUB) & 1 : 0;
-        if (!SSM_FWD_PREF) fetch(0, t0s);
-        if (SSM_FWD_PREF && t0s + SSM_FWD_SUB < TC) fetch(cur ^ 1, t0s + SSM_FWD_SUB);
-        float2 av[SSM_FWD_SUB][NP], bv[SSM_FWD_SUB][NP], cv[SSM_FWD_SUB][NP];
-        float yd[SSM_FWD_SUB];
+      for (int t0s = 0; t0s < TC; t0s += kFwdSub) {
+        const int cur = (t0s / kFwdSub) & 1;
+        if (t0s + kFwdSub < TC) fetch(cur ^ 1, t0s + kFwdSub);
+        float2 av[kFwdSub][NP], bv[kFwdSub][NP], cv[kFwdSub][NP];
 #pragma unroll
-        for (int q = 0; q < SSM_FWD_SUB; ++q) {
-          const int tt = t0s + q;
+        for (int q = 0; q < kFwdSub; ++q) {
           const float uu = fu[cur][q];
           const float dtv = fdt[cur][q];
           const float2 u2 = bc2(uu), dt2 = bc2(dtv), dtu2 = bc2(dtv * uu);
@@ -378,30 +354,25 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
             Bn[i] = fB[cur][q][i];
             cv[q][i] = fC[cur][q][i];
           }
-          yd[q] = SSM_FWD_LATEZ ? 0.0f : Dd0 * uu;
 #pragma unroll
           for (int i = 0; i < NP; ++i)
             fwd_coeffs2<METHOD>(dt2, u2, dtu2, Bn[i], Ak[i], A2[i], niA[i], av[q][i], bv[q][i]);
-          if (MODE == kModeMain && !SSM_FWD_LATEZ) {   // branch-free: without z the tiles hold zeros
-            const float zz = to_f32(Zs[tt * BXC + dl]);
-            if (g == tt % LPC) zk[tt / LPC] = zz;
-          }
         }
 #pragma unroll
-        for (int q = 0; q < SSM_FWD_SUB; ++q) {
+        for (int q = 0; q < kFwdSub; ++q) {
           const int tt = t0s + q;
-          float2 acc = make_float2(yd[q], 0.f);
+          float2 acc = bc2(0.f);
 #pragma unroll
           for (int i = 0; i < NP; ++i) {
             h[i] = fwd_apply2<METHOD>(h[i], av[q][i], bv[q][i]);
-            if (MODE == kModeMain) acc = (SSM_FWD_LATEZ && i == 0) ? mul2(cv[q][i], h[i]) : fma2(cv[q][i], h[i], acc);
+            if (MODE == kModeMain) acc = (i == 0) ? mul2(cv[q][i], h[i]) : fma2(cv[q][i], h[i], acc);
             else P[i] = mul2(P[i], av[q][i]);
           }
           yp[(tt % LPC) * YPL + tt / LPC] = acc.x + acc.y;
         }
-        if (SSM_FWD_PIPE && MODE == kModeMain && t0s == (TC > SSM_FWD_SUB ? SSM_FWD_SUB : 0)) emit(ypv, zpv, upv, tpv);
+        if (MODE == kModeMain && t0s == (TC > kFwdSub ? kFwdSub : 0)) emit(ypv, zpv, upv, tpv);
       }
-      if (MODE == kModeMain && SSM_FWD_LATEZ) {   // z and u of the lane's output steps, before the refill
+      if (MODE == kModeMain) {   // z and u of the lane's output steps, before the refill
 #pragma unroll
         for (int i = 0; i < YPL; ++i) {
           zk[i] = to_f32(Zs[(g + i * LPC) * BXC + dl]);
@@ -416,23 +387,19 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
       fwd_issue_loads<S, MODE>(p, st, &bars[s], x0, box_t0(q + S::NSTAGE), b);
 
     if (MODE == kModeMain) {
-      if (SSM_FWD_PIPE) {
 #pragma unroll
-        for (int i = 0; i < TC; ++i) ypv[i] = yp[i];
+      for (int i = 0; i < TC; ++i) ypv[i] = yp[i];
 #pragma unroll
-        for (int i = 0; i < YPL; ++i) {
-          zpv[i] = zk[i];
-          upv[i] = uk[i];
-        }
-        tpv = t0;
-      } else {
-        emit(yp, zk, uk, t0);
+      for (int i = 0; i < YPL; ++i) {
+        zpv[i] = zk[i];
+        upv[i] = uk[i];
       }
+      tpv = t0;
     }
   }
 
   if (MODE == kModeMain) {
-    if (SSM_FWD_PIPE) emit(ypv, zpv, upv, tpv);
+    emit(ypv, zpv, upv, tpv);
     if (dvalid && t_end == p.L && p.last != nullptr) storep<G>(p.last + ((size_t)b * p.D + d) * N + nbase, h);
   } else if (dvalid) {
     const size_t o = (((size_t)b * p.nseg + seg) * p.D + d) * N + nbase;
