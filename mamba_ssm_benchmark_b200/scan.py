@@ -37,6 +37,9 @@ def _validate(x, delta, A, Bm, Cm, method):
     if x.dim() != 3 or delta.shape != x.shape:
         raise ValueError(f"x and delta must be (B, L, D) of equal shape, got {tuple(x.shape)} / {tuple(delta.shape)}")
     Bsz, L, D = x.shape
+    if min(Bsz, L, D) < 1:
+        raise ValueError(f"x must have positive B, L and D, got {tuple(x.shape)} (the reference fails on "
+                         f"empty inputs too)")
     if A.dim() != 2 or A.shape[0] != D:
         raise ValueError(f"A must be (D, N) with D={D}, got {tuple(A.shape)}")
     N = A.shape[1]

@@ -83,3 +83,7 @@ def test_python_api_rejects_like_the_reference():
         selective_scan(x, x, A, Bm, Bm, scan="chunked")
     with pytest.raises(RuntimeError, match="CUDA"):
         selective_scan_triton(x, x, A, Bm, Bm)
+    for shape in ((1, 0, 8), (0, 4, 8)):
+        e = torch.zeros(*shape)
+        with pytest.raises(ValueError, match="positive"):
+            selective_scan_triton(e, e, A, torch.zeros(shape[0], shape[1], 16), torch.zeros(shape[0], shape[1], 16))

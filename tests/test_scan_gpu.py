@@ -144,6 +144,19 @@ def test_bf16_activations(shape):
     assert got["du"].dtype == torch.bfloat16 and got["dA"].dtype == torch.float32
 
 
+@pytest.mark.parametrize("B, L, D", [(2, 0, 8), (0, 16, 8), (2, 16, 0)])
+def test_empty_shapes_raise_value_error(B, L, D):
+    """Empty inputs are rejected cleanly (the reference fails on them too: ZeroDivisionError in
+    models/scan.py's chunked scan); no kernel is launched."""
+    x = torch.zeros(B, L, D, device=DEV)
+    A = -torch.ones(D, 16, device=DEV)
+    Bm = torch.zeros(B, L, 16, device=DEV)
+    with pytest.raises(ValueError):
+        selective_scan(x, x, A, Bm, Bm)
+    with pytest.raises(ValueError):
+        selective_scan_fused(x, x, A, Bm, Bm, D=torch.ones(D, device=DEV), z=x)
+
+
 def test_mixed_dtypes_are_promoted_like_the_reference():
     ins = make_inputs(2, 40, 32, 16, seed=9, dist="test")
     x = ins["u"].to(DEV, torch.bfloat16)
