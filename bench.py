@@ -197,17 +197,35 @@ def e2e_run(cfg, device, steps, world, seed):
     forward and backward through selective_scan_fused + autograd, and copies every output back to
     pinned host memory.  The copies run on their own streams with double-buffered device inputs, so
     step i's device-to-host copy and step i+1's host-to-device copy overlap step i's compute.
+    Each direction is one copy per step: the inputs sit in one pinned staging buffer (one
+    256-byte-aligned slot per tensor, the device tensors are views of its device twin), and the
+    outputs are gathered on the device into one contiguous byte buffer before their download.
+    Measured on a B200, one copy each way instead of one per tensor (9 up, 10 down) took
+    1.48-1.64 ms per config-1 step against 1.71-2.01 ms.
     A step's outputs are held until the step two later, whose compute first waits for their
     device-to-host copy, so the allocator reuses their blocks in stream order (recording them
     on the copy stream instead kept the allocator growing with fresh device allocations)."""
     from mamba_ssm_benchmark_b200 import selective_scan_fused, sharding
     from mamba_ssm_benchmark_b200.workloads import make_inputs
     ins = make_inputs(cfg.B, cfg.L, cfg.D, cfg.N, seed=seed, dist="config", dtype=cfg.dtype)
-    host = {k: v.pin_memory() for k, v in ins.items() if v is not None}
-    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    names = [k for k, v in ins.items() if v is not None]
+    offs, total = {}, 0
+    for n in names:
+        offs[n] = total
+        total += (ins[n].numel() * ins[n].element_size() + 255) // 256 * 256
+    staging = torch.empty(total, dtype=torch.uint8).pin_memory()
+
+    def views(buf):
+        return {n: buf[offs[n]:offs[n] + ins[n].numel() * ins[n].element_size()].view(ins[n].dtype).view(ins[n].shape)
+                for n in names}
+
+    for n, v in views(staging).items():
+        v.copy_(ins[n])
+    h2d = total                                   # the whole staging buffer, alignment padding included
     compute = torch.cuda.current_stream(device)
     up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    dev_sets = [{k: torch.empty(v.shape, dtype=v.dtype, device=device) for k, v in host.items()} for _ in range(2)]
+    dev_bufs = [torch.empty(total, dtype=torch.uint8, device=device) for _ in range(2)]
+    dev_sets = [views(buf) for buf in dev_bufs]
     up_done = [torch.cuda.Event() for _ in range(2)]
     comp_done = [torch.cuda.Event() for _ in range(2)]
     down_done = [torch.cuda.Event() for _ in range(2)]
@@ -218,8 +236,7 @@ def e2e_run(cfg, device, steps, world, seed):
     def upload(k):
         up.wait_event(comp_done[k])               # the compute that last read this set is done
         with torch.cuda.stream(up):
-            for n, v in host.items():
-                dev_sets[k][n].copy_(v, non_blocking=True)
+            dev_bufs[k].copy_(staging, non_blocking=True)
         up_done[k].record(up)
 
     def compute_step(k):
@@ -235,16 +252,16 @@ def e2e_run(cfg, device, steps, world, seed):
         if world > 1:
             sharding.reduce_shared_grads(grads[3:5])          # dBm, dCm: partial sums over channel shards
         res = [y.detach(), last.detach()] + grads
+        packed = torch.cat([r.contiguous().view(-1).view(torch.uint8) for r in res])   # one download
         comp_done[k].record(compute)
         if outs_host[k] is None:
-            outs_host[k] = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+            outs_host[k] = torch.empty(packed.numel(), dtype=torch.uint8, pin_memory=True)
         down.wait_event(comp_done[k])
         with torch.cuda.stream(down):
-            for o, r in zip(outs_host[k], res):
-                o.copy_(r, non_blocking=True)
+            outs_host[k].copy_(packed, non_blocking=True)
         down_done[k].record(down)
-        held[k] = res
-        d2h = sum(r.numel() * r.element_size() for r in res)
+        held[k] = packed
+        d2h = packed.numel()
 
     def run(n):
         upload(0)
