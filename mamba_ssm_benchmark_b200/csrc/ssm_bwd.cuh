@@ -159,6 +159,8 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
   float* __restrict__ SCP = reinterpret_cast<float*>(smem + S::OFF_CP);
   float* __restrict__ SRED = reinterpret_cast<float*>(smem + S::OFF_RED);
   float* __restrict__ SDD = reinterpret_cast<float*>(smem + S::OFF_DD);
+  pdl_launch_dependents();
+  pdl_wait();
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = lane / LPC, g = lane % LPC;
@@ -624,6 +626,8 @@ __global__ void ssm_bwd_finalize(const FinParams p) {
     }
     return s;
   };
+  pdl_launch_dependents();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const long long gtid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   const long long nthr = (long long)gridDim.x * blockDim.x;

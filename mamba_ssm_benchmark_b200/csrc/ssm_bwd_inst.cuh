@@ -13,8 +13,7 @@ static cudaError_t launch_bwd_nm(const BwdParams& p, dim3 grid, cudaStream_t str
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
   }
-  kern<<<grid, Geo<N, G>::NT, smem, stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(kern, grid, dim3(Geo<N, G>::NT), smem, stream, p);
 }
 
 template <typename T, int N, int G>
@@ -55,8 +54,7 @@ cudaError_t launch_bwd_finalize<SSM_ELEM>(const FinParams& p, cudaStream_t strea
   const long long rest = ((long long)p.D * p.N + 2LL * p.D + 255) / 256;
   if (blocks < rest) blocks = rest;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  ssm_bwd_finalize<SSM_ELEM><<<(unsigned)blocks, 256, 0, stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(ssm_bwd_finalize<SSM_ELEM>, dim3((unsigned)blocks), dim3(256), 0, stream, p);
 }
 
 }  // namespace ssm

@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace ssm {
 
 constexpr float kLog2e = 1.4426950408889634f;
@@ -200,6 +202,32 @@ __device__ __forceinline__ void store_tile(const T* tile, const DAct& v, int b, 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+// Programmatic dependent launch.  A kernel launched with launch_pdl may be scheduled while the
+// kernel before it in the stream is still draining.  Every such kernel calls pdl_wait() before its
+// first global-memory access (read or write): it returns once the previous kernel has completed
+// and its writes are visible, so the kernel sees exactly what a plain launch would see.
+// pdl_launch_dependents() at a kernel's top lets the next launch_pdl kernel be scheduled once all
+// of this grid's CTAs are running.  Kernels from other libraries that follow are launched
+// normally.  Measured at config 1 (fwd + bwd + finalize): 173.3 -> 171.3 us per step.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }

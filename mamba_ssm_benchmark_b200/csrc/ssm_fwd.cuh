@@ -137,6 +137,8 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
   constexpr int YPL = TC / LPC;   // output steps per lane after the y reduction
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
+  pdl_launch_dependents();
+  pdl_wait();
 
   // Lane layout: state group major.  The 8 lanes of a quarter warp then share one state group,
   // so the vector loads of B and C read one address per quarter warp (a broadcast) instead of

@@ -18,8 +18,7 @@ static cudaError_t launch_fwd_nm(const FwdParams& p, dim3 grid, cudaStream_t str
   // one warp per CTA; grid.x counts CPW-channel slices
   dim3 g2(grid);
   g2.x = (unsigned)((p.D + Geo<N, G>::CPW - 1) / Geo<N, G>::CPW);
-  kern<<<g2, 32, smem, stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(kern, g2, dim3(32), smem, stream, p);
 }
 
 template <typename T, int N, int G, int MODE, int KB>

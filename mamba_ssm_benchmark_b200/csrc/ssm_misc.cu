@@ -9,6 +9,8 @@ namespace ssm {
 // The chunk-level combine of the reference's two-level scan (models/scan.py:160-164, whose
 // log-depth Hillis-Steele pass over chunk ends is replaced by this O(S) walk per state).
 __global__ void ssm_carry_kernel(const CarryParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   const long long dn_total = (long long)p.D * p.N;
   const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (idx >= (long long)p.B * dn_total) return;
@@ -31,8 +33,7 @@ __global__ void ssm_carry_kernel(const CarryParams p) {
 
 cudaError_t launch_carry(const CarryParams& p, cudaStream_t stream) {
   const long long total = (long long)p.B * p.D * p.N;
-  ssm_carry_kernel<<<(unsigned)((total + 127) / 128), 128, 0, stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(ssm_carry_kernel, dim3((unsigned)((total + 127) / 128)), dim3(128), 0, stream, p);
 }
 
 // Single-token state update: the inline decode branch of Mamba.forward
