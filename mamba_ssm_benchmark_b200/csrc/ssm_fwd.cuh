@@ -233,6 +233,10 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
 #pragma unroll
   for (int i = 0; i < TC / LPC; ++i) zpv[i] = upv[i] = 0.f;
 
+  // Two tiles per loop trip: the hand-over of a tile's outputs to the next trip (ypv = yp, ...)
+  // then becomes register renaming instead of 24 moves per tile (96 -> 114 registers; config 1
+  // forward 49.25 -> 47.3 us, step 171.1 -> 169.2 us, same box).
+#pragma unroll 2
   for (int k = 0; k < nblk; ++k) {
     const int tix = (MODE == kModeAdjoint) ? nblk - 1 - k : k;     // tile within the segment
     const int bx = tix / KB, sub = tix % KB;
