@@ -140,8 +140,9 @@ SSM_API int ssm_scan_bwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t met
  * loads the library, held until the process exits.  Shapes whose backward needs more
  * scratch than that (ssm_scan_bwd_workspace_size) are rejected with SSM_ERR_WORKSPACE and
  * a message naming both sizes.  The call allocates nothing.
- *   - The first call on a device looks up the array's device address once for that
- *     device (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - Every call looks up the array's device address on the current device
+ *     (cudaGetSymbolAddress); the first call on a device may load the library's module
+ *     there, so make that first call before any stream capture.
  *   - Every call shares the one array and leaves its contents behind (the backward
  *     overwrites everything it reads, so nothing needs clearing).  Calls that overlap on
  *     the GPU — concurrent streams, or several host threads — race on it: serialise them.

@@ -12,9 +12,9 @@ torch tensors into it.  Build it with ``python -m mamba_ssm_benchmark_b200.build
 
 from .conv import causal_conv1d
 from .decode import selective_state_update
-from .scan import (FUSED_SCANS, SUPPORTED_N, SelectiveScanFn, selective_scan, selective_scan_fused,
+from .scan import (SCAN_NAMES, SUPPORTED_N, SelectiveScanFn, selective_scan, selective_scan_fused,
                    selective_scan_triton)
 
 __all__ = ["selective_scan", "selective_scan_triton", "selective_scan_fused", "selective_state_update",
-           "causal_conv1d", "SelectiveScanFn", "FUSED_SCANS", "SUPPORTED_N"]
+           "causal_conv1d", "SelectiveScanFn", "SCAN_NAMES", "SUPPORTED_N"]
 __version__ = "0.1.0"

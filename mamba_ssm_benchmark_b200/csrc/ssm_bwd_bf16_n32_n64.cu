@@ -1,0 +1,8 @@
+// Backward selective-scan kernels, bfloat16 activations, N in {32, 64}.
+#define SSM_BWD_INSTANTIATE
+#include "ssm_bwd_inst.cuh"
+
+namespace ssm {
+template cudaError_t launch_bwd_n<__nv_bfloat16, 32, 4>(int, const BwdParams&, dim3, cudaStream_t);
+template cudaError_t launch_bwd_n<__nv_bfloat16, 64, 4>(int, const BwdParams&, dim3, cudaStream_t);
+}  // namespace ssm

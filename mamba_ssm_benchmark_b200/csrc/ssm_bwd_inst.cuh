@@ -1,9 +1,18 @@
-// ssm_bwd_inst.cuh — instantiates and dispatches the backward kernels for one element type
-// (SSM_ELEM, set by the including translation unit).
+// ssm_bwd_inst.cuh — backward kernel instantiation and dispatch for one element type.
+//
+// As for the forward: ssm_bwd_<type>_n<...>.cu instantiate launch_bwd_n for their N (with
+// SSM_BWD_INSTANTIATE defined); ssm_bwd_<type>.cu (SSM_ELEM set) holds the dispatcher and the
+// finalize kernel.
 #pragma once
 #include "ssm_bwd.cuh"
 
 namespace ssm {
+
+// Launches the backward kernel of one (element type, N, G) for any method.
+template <typename T, int N, int G>
+cudaError_t launch_bwd_n(int method, const BwdParams& p, dim3 grid, cudaStream_t stream);
+
+#ifdef SSM_BWD_INSTANTIATE
 
 template <typename T, int N, int G, int METHOD>
 static cudaError_t launch_bwd_nm(const BwdParams& p, dim3 grid, cudaStream_t stream) {
@@ -17,7 +26,7 @@ static cudaError_t launch_bwd_nm(const BwdParams& p, dim3 grid, cudaStream_t str
 }
 
 template <typename T, int N, int G>
-static cudaError_t launch_bwd_n(int method, const BwdParams& p, dim3 grid, cudaStream_t stream) {
+cudaError_t launch_bwd_n(int method, const BwdParams& p, dim3 grid, cudaStream_t stream) {
   switch (method) {
     case kZOH: return launch_bwd_nm<T, N, G, kZOH>(p, grid, stream);
     case kEuler: return launch_bwd_nm<T, N, G, kEuler>(p, grid, stream);
@@ -25,6 +34,8 @@ static cudaError_t launch_bwd_n(int method, const BwdParams& p, dim3 grid, cudaS
   }
   return cudaErrorInvalidValue;
 }
+
+#else
 
 // G = 2 (twice the threads for small grids) is built for N = 8 and 16.
 template <>
@@ -56,5 +67,7 @@ cudaError_t launch_bwd_finalize<SSM_ELEM>(const FinParams& p, cudaStream_t strea
   if (blocks > 148 * 16) blocks = 148 * 16;
   return launch_pdl(ssm_bwd_finalize<SSM_ELEM>, dim3((unsigned)blocks), dim3(256), 0, stream, p);
 }
+
+#endif  // SSM_BWD_INSTANTIATE
 
 }  // namespace ssm

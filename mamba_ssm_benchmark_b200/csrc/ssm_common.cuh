@@ -107,6 +107,36 @@ __device__ __forceinline__ void storep(float* p, const float2 (&v)[G / 2]) {
   else *reinterpret_cast<float2*>(p) = v[0];
 }
 
+// 2^x - 1 for a pair, given a = ex2(x) from the MUFU: the ZOH input coefficient
+// expm1(delta A) (models/scan.py:50 uses torch.expm1), accurate in relative terms also where |x|
+// is small.  a - 1 alone is not: ex2.approx's absolute error near 1 (about 1e-7) becomes a
+// relative error of about 1e-7 / |delta A| in expm1, 1e-3 at |delta A| = 1e-4.
+// Both candidates are lower bounds of e^z - 1 (z = x ln 2) for every x:
+//   * the third-order Taylor polynomial z + z^2/2 + z^3/6 (Lagrange remainder e^xi z^4/24 >= 0);
+//   * the MUFU value scaled down by (1 - 2^-22), more than ex2.approx's relative error (measured
+//     on B200 against double-precision exp2: at most 1.46e-7 = 2^-22.7 over every float in
+//     [-1, 1] and a sample of [-126, 64)), minus 1.
+// Their maximum is therefore within min(z^4/24, 3.9e-7 e^z) of e^z - 1: the polynomial wins for
+// small |z|, the MUFU value for large |z|, and the worst relative error (|z| near 0.055) is about
+// 7e-6.  Five FP operations per pair beyond a - 1; no branch, no division.
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kEm1C1 = kLn2;                                 // ln2
+constexpr float kEm1C2 = 0.2402265069591007f;                  // ln2^2 / 2
+constexpr float kEm1C3 = 0.05550410866482158f;                 // ln2^3 / 6
+constexpr float kEm1Scale = 1.0f - 2.384185791015625e-7f;      // 1 - 2^-22
+__device__ __forceinline__ float2 em1x2(float2 x, float2 a) {
+  const float2 e = fma2(a, bc2(kEm1Scale), bc2(-1.0f));
+  float2 p = fma2(x, bc2(kEm1C3), bc2(kEm1C2));
+  p = fma2(x, p, bc2(kEm1C1));
+  const float2 s = mul2(x, p);
+  return make_float2(fmaxf(s.x, e.x), fmaxf(s.y, e.y));
+}
+__device__ __forceinline__ float em1x(float x, float a) {
+  const float e = fmaf(a, kEm1Scale, -1.0f);
+  const float s = x * fmaf(x, fmaf(x, kEm1C3, kEm1C2), kEm1C1);
+  return fmaxf(s, e);
+}
+
 // logistic sigmoid from e^-z = 2^(-z log2 e)
 __device__ __forceinline__ float sigmoid(float z) { return rcp(1.0f + ex2(-z * kLog2e)); }
 // softplus(x) = log(1 + e^x) with torch's default threshold (x > 20 returns x), the step-size

@@ -55,18 +55,16 @@ struct FwdSmem {
 };
 
 // Discretization of one step for a pair of states, split into the state-independent
-// coefficients (phase A) and the update (phase B).  ZOH: b = expm1(dt A)/A B u is applied as
-// h' = a (h + g) - g with g = B u / A; the coefficient kept is ng = -g (so both uses are one
-// packed FMA): h + g = fma(ng, -1, h), h' = fma(a, h + g, ng).  Euler and bilinear use
-// h' = a h + b.
+// coefficients (phase A) and the update (phase B), h' = a h + b for every method.  ZOH:
+// b = expm1(dt A) / A * B u with expm1 from em1x2 (accurate also for small |dt A|).
 
 template <int METHOD>
 __device__ __forceinline__ void fwd_coeffs2(float2 dt2, float2 u2, float2 dtu2, float2 B2, float2 Ak2, float2 A2k2,
-                                            float2 niA2, float2& a, float2& bco) {
+                                            float2 iA2, float2& a, float2& bco) {
   if (METHOD == kZOH) {
-    a = ex2x2(mul2(dt2, A2k2));
-    bco = mul2(mul2(B2, u2), niA2);
-    bco = fma2(bco, make_float2(-a.x, -a.y), bco);   // b = g (1 - a): one FMA per step on the chain
+    const float2 x = mul2(dt2, A2k2);
+    a = ex2x2(x);
+    bco = mul2(em1x2(x, a), mul2(mul2(B2, u2), iA2));
   } else if (METHOD == kEuler) {
     a = ex2x2(mul2(dt2, A2k2));
     bco = mul2(dtu2, B2);
@@ -160,9 +158,9 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
   const int nbox = (nblk + KB - 1) / KB;
   auto box_t0 = [&](int q) { return t_begin + ((MODE == kModeAdjoint) ? nbox - 1 - q : q) * S::TB; };
 
-  // Per-state constants, as pairs: A, A log2(e) (for 2^x), -1/A.  Channels past D get A = -1
+  // Per-state constants, as pairs: A, A log2(e) (for 2^x), 1/A.  Channels past D get A = -1
   // and zero inputs.
-  float2 Ak[NP], A2[NP], niA[NP];
+  float2 Ak[NP], A2[NP], iA[NP];
   {
     float av[G];
 #pragma unroll
@@ -172,7 +170,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
     for (int i = 0; i < NP; ++i) {
       Ak[i] = make_float2(av[2 * i], av[2 * i + 1]);
       A2[i] = mul2(Ak[i], bc2(kLog2e));
-      niA[i] = make_float2(-1.0f / av[2 * i], -1.0f / av[2 * i + 1]);
+      iA[i] = make_float2(1.0f / av[2 * i], 1.0f / av[2 * i + 1]);
     }
   }
   // D skip, added to the reduced y of the lane's output steps
@@ -310,7 +308,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
 #pragma unroll
           for (int i = 0; i < NP; ++i) {
             float2 unused;
-            fwd_coeffs2<METHOD>(dt2, bc2(0.f), bc2(0.f), Cn[i], Ak[i], A2[i], niA[i], av[q][i], unused);
+            fwd_coeffs2<METHOD>(dt2, bc2(0.f), bc2(0.f), Cn[i], Ak[i], A2[i], iA[i], av[q][i], unused);
             cd[q][i] = mul2(av[q][i], mul2(Cn[i], dys2));
           }
         }
@@ -362,7 +360,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
           }
 #pragma unroll
           for (int i = 0; i < NP; ++i)
-            fwd_coeffs2<METHOD>(dt2, u2, dtu2, Bn[i], Ak[i], A2[i], niA[i], av[q][i], bv[q][i]);
+            fwd_coeffs2<METHOD>(dt2, u2, dtu2, Bn[i], Ak[i], A2[i], iA[i], av[q][i], bv[q][i]);
         }
 #pragma unroll
         for (int q = 0; q < kFwdSub; ++q) {

@@ -1,3 +1,3 @@
-// Forward selective-scan kernels, bfloat16 activations (float32 state and accumulation).
+// Forward selective-scan dispatch, bfloat16 activations (kernels: ssm_fwd_bf16_n*.cu).
 #define SSM_ELEM __nv_bfloat16
 #include "ssm_fwd_inst.cuh"

@@ -1,0 +1,9 @@
+// Forward selective-scan kernels, float32 activations, N in {4, 8}.
+#define SSM_FWD_INSTANTIATE
+#include "ssm_fwd_inst.cuh"
+
+namespace ssm {
+template cudaError_t launch_fwd_n<float, 4, 4>(int, int, int, const FwdParams&, dim3, cudaStream_t);
+template cudaError_t launch_fwd_n<float, 8, 4>(int, int, int, const FwdParams&, dim3, cudaStream_t);
+template cudaError_t launch_fwd_n<float, 8, 2>(int, int, int, const FwdParams&, dim3, cudaStream_t);
+}  // namespace ssm

@@ -1,11 +1,20 @@
-// ssm_fwd_inst.cuh — instantiates and dispatches the forward kernels for one element type
-// (SSM_ELEM, set by the including translation unit).
+// ssm_fwd_inst.cuh — forward kernel instantiation and dispatch for one element type.
+//
+// The kernels of one (element type, N, G) are instantiated by their own translation unit
+// (ssm_fwd_<type>_n<N>.cu defines SSM_FWD_INSTANTIATE and instantiates launch_fwd_n), so the
+// compiler builds them in parallel; ssm_fwd_<type>.cu (SSM_ELEM set) holds the dispatcher.
 #pragma once
 #include <type_traits>
 
 #include "ssm_fwd.cuh"
 
 namespace ssm {
+
+// Launches the forward kernel of one (element type, N, G) for any method, mode and box size.
+template <typename T, int N, int G>
+cudaError_t launch_fwd_n(int method, int mode, int kb, const FwdParams& p, dim3 grid, cudaStream_t stream);
+
+#ifdef SSM_FWD_INSTANTIATE
 
 template <typename T, int N, int G, int METHOD, int MODE, int KB>
 static cudaError_t launch_fwd_nm(const FwdParams& p, dim3 grid, cudaStream_t stream) {
@@ -34,7 +43,7 @@ static cudaError_t launch_fwd_m(int method, const FwdParams& p, dim3 grid, cudaS
 // The main pass exists with 2- and 4-tile boxes; the summary and adjoint passes (split sequences,
 // short segments) use 2-tile boxes.
 template <typename T, int N, int G>
-static cudaError_t launch_fwd_n(int method, int mode, int kb, const FwdParams& p, dim3 grid, cudaStream_t stream) {
+cudaError_t launch_fwd_n(int method, int mode, int kb, const FwdParams& p, dim3 grid, cudaStream_t stream) {
   if (mode == kModeMain)
     return kb == 4 ? launch_fwd_m<T, N, G, kModeMain, 4>(method, p, grid, stream)
                    : launch_fwd_m<T, N, G, kModeMain, 2>(method, p, grid, stream);
@@ -42,6 +51,8 @@ static cudaError_t launch_fwd_n(int method, int mode, int kb, const FwdParams& p
   if (mode == kModeAdjoint) return launch_fwd_m<T, N, G, kModeAdjoint, 2>(method, p, grid, stream);
   return cudaErrorInvalidValue;
 }
+
+#else
 
 // G = 2 (twice the threads for small grids) is built for N = 8 and 16.
 template <>
@@ -82,5 +93,7 @@ int fwd_smem_bytes<SSM_ELEM>(int N, int G, int kb) {
     default: return pick(std::integral_constant<int, 64>{}, I4{});
   }
 }
+
+#endif  // SSM_FWD_INSTANTIATE
 
 }  // namespace ssm

@@ -70,8 +70,9 @@ __global__ void __launch_bounds__(128) ssm_update_kernel(const UpdParams p) {
     const float z = dtv * Ak[k];
     float a, bb;
     if (p.method == kZOH) {
-      a = ex2(z * kLog2e);
-      bb = (a - 1.0f) / Ak[k] * (Bn[k] * xv);
+      const float x = z * kLog2e;
+      a = ex2(x);
+      bb = em1x(x, a) / Ak[k] * (Bn[k] * xv);   // expm1(delta A) / A B x, accurate for small |delta A|
     } else if (p.method == kEuler) {
       a = ex2(z * kLog2e);
       bb = dtv * (Bn[k] * xv);

@@ -7,13 +7,12 @@
 // holds SSM_NOALLOC_SCRATCH_BYTES of device memory until the process exits.
 //
 // The scratch is a file-scope __device__ array.  Host code must not pass the array's name to a
-// kernel (in host code it is only a host-side stand-in); its device address is looked up once
-// per device, with that device current, through cudaGetSymbolAddress on the first call made on
-// that device, and cached.
+// kernel (in host code it is only a host-side stand-in); every call looks up its device address
+// on the current device through cudaGetSymbolAddress (cheap once the module is loaded; not cached,
+// so a cudaDeviceReset, after which the array can sit elsewhere, leaves no stale address behind).
 #include <cuda_runtime.h>
 
 #include <cstdio>
-#include <mutex>
 
 #include "ssm_b200.h"
 
@@ -25,32 +24,16 @@ namespace {
 
 static __device__ __align__(256) unsigned char g_ssm_noalloc_scratch[SSM_NOALLOC_SCRATCH_BYTES];
 
-// Device address of the scratch array on the current device (set up on first use per device).
+// Device address of the scratch array on the current device.
 int scratch_address(void** out) {
-  static std::mutex mu;
-  static void* addr[64] = {nullptr};
   char msg[256];
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_ssm_noalloc_scratch);
   if (e != cudaSuccess) {
-    snprintf(msg, sizeof(msg), "cudaGetDevice: %s", cudaGetErrorString(e));
+    snprintf(msg, sizeof(msg), "cudaGetSymbolAddress of the scratch array: %s", cudaGetErrorString(e));
     return ssm::report_error(SSM_ERR_CUDA, msg);
   }
-  if (dev < 0 || dev >= 64) {
-    snprintf(msg, sizeof(msg), "device %d out of range", dev);
-    return ssm::report_error(SSM_ERR_UNSUPPORTED, msg);
-  }
-  std::lock_guard<std::mutex> lk(mu);
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_ssm_noalloc_scratch);
-    if (e != cudaSuccess) {
-      snprintf(msg, sizeof(msg), "cudaGetSymbolAddress of the scratch array: %s", cudaGetErrorString(e));
-      return ssm::report_error(SSM_ERR_CUDA, msg);
-    }
-    addr[dev] = p;
-  }
-  *out = addr[dev];
+  *out = p;
   return SSM_OK;
 }
 

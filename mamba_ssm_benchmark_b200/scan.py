@@ -4,11 +4,14 @@ Reference interfaces this module keeps (same argument names, meaning and errors)
 
 * ``selective_scan_triton(x, delta, A, Bm, Cm, h0=None, method="zoh", d_block=None)``
   — kernels/triton_scan.py:322-329, the fused-kernel entry point, returning ``(y, last)``.
-* ``selective_scan(x, delta, A, Bm, Cm, h0=None, method="zoh", scan=..., d_block=None,
+* ``selective_scan(x, delta, A, Bm, Cm, h0=None, method="zoh", scan="chunked", d_block=None,
   chunk_size=None)`` — models/scan.py:277-299, the dispatcher the Mamba mixer calls
-  (models/mamba.py:120-121).  Here every scan name that selects the fused GPU path
-  ("auto", "triton", "b200", "cuda") runs the sm_100a kernels; names of the reference's
-  PyTorch scans raise, because this package ships no non-CUDA path.
+  (models/mamba.py:120-121), with the reference's default.  Every scan name the reference
+  accepts ("chunked", "sequential", "hillis_steele", "blelloch", "reference", "triton", "auto")
+  names an algorithm for the same function, the selective scan; on CUDA tensors each of them
+  runs the sm_100a kernels (there is one implementation here, no dispatch between backends),
+  and on CPU tensors every one raises, because this package ships no non-CUDA path.  An
+  unknown name raises ValueError.
 
 Extension: ``D=`` and ``z=`` fuse the mixer's skip and gate, ``(y + x*D) * silu(z)``
 (models/mamba.py:124), into the same kernels.
@@ -25,8 +28,8 @@ import torch
 
 from . import _native as nat
 
-FUSED_SCANS = ("auto", "triton", "b200", "cuda")
-REFERENCE_ONLY_SCANS = ("reference", "sequential", "hillis_steele", "blelloch", "chunked")
+# scan names of the reference (models/scan.py:280-282) plus this package's own; all select the fused kernels
+SCAN_NAMES = ("chunked", "sequential", "hillis_steele", "blelloch", "reference", "triton", "auto", "b200", "cuda")
 SUPPORTED_N = (4, 8, 16, 32, 64)
 CHUNK = 16  # checkpoint interval of the forward's saved states (time steps)
 
@@ -180,18 +183,16 @@ def selective_scan_triton(x, delta, A, Bm, Cm, h0=None, method="zoh", d_block=No
     return selective_scan_fused(x, delta, A, Bm, Cm, h0=h0, method=method)
 
 
-def selective_scan(x, delta, A, Bm, Cm, h0=None, method="zoh", scan="auto", d_block=None, chunk_size=None):
-    """Drop-in for models/scan.py:selective_scan on the fused GPU path.
+def selective_scan(x, delta, A, Bm, Cm, h0=None, method="zoh", scan="chunked", d_block=None, chunk_size=None):
+    """Drop-in for models/scan.py:selective_scan: returns (y, h_last).
 
-    Returns (y, h_last).  x, delta: (B, L, D); A: (D, N); Bm, Cm: (B, L, N); h0: (B, D, N).
+    x, delta: (B, L, D); A: (D, N); Bm, Cm: (B, L, N); h0: (B, D, N).  ``scan`` may be any name the
+    reference accepts; all of them compute the selective scan and run the fused sm_100a kernels.
     ``chunk_size`` and ``d_block`` only tune the reference's PyTorch scans and are ignored.
     """
     del chunk_size
-    if scan in REFERENCE_ONLY_SCANS:
-        raise ValueError(f"scan={scan!r} selects the reference's PyTorch scan, which this package does not "
-                         f"ship; use one of {FUSED_SCANS}")
-    if scan not in FUSED_SCANS:
-        raise ValueError(f"unknown scan {scan!r}; expected one of {FUSED_SCANS}")
+    if scan not in SCAN_NAMES:
+        raise ValueError(f"unknown scan {scan!r}; expected one of {SCAN_NAMES}")
     with torch.autocast(device_type="cuda", enabled=False):
         return selective_scan_triton(x, delta, A, Bm, Cm, h0=h0, method=method, d_block=d_block)
 

@@ -26,6 +26,8 @@ the full backward of its shard with its incoming adjoint (the reverse adjoint of
 models/scan.py:239-240, carried across shards).
 """
 
+import time
+
 import torch
 import torch.distributed as dist
 
@@ -205,6 +207,61 @@ def compose_suffix(decays, dstarts, dlast=None):
     return dl_in, g
 
 
+# ------------------------------------------------------------------------------------------------
+# failure detection between the steps of a sharded scan (host side)
+# ------------------------------------------------------------------------------------------------
+class PeerLost(RuntimeError):
+    """A rank of the group did not reach a step of the sharded scan within the timeout."""
+
+    def __init__(self, step, missing, timeout):
+        super().__init__(f"rank(s) {missing} did not reach step {step} of the sharded scan within {timeout:.1f} s")
+        self.step, self.missing = step, missing
+
+
+class PeerCheck:
+    """Host-side liveness check before every exchange of a sharded scan.
+
+    Every rank announces step k in the process group's key-value store, then waits until all
+    ranks have, for at most ``timeout`` seconds, polling the store (no GPU work and no collective).
+    A rank that died, left, or hangs before step k makes the others raise ``PeerLost`` naming it
+    before they enter the step's collective; a collective that a peer never joins would otherwise
+    block until the process group's own timeout, with the caller's kernels already queued behind
+    it.  A late rank (within the timeout) only delays the others.  Steps are numbered by the
+    check itself, so every rank must call ``step()`` the same number of times, in the same order,
+    as it does the collectives.  Keys of step k - 2 are deleted once step k is reached."""
+
+    def __init__(self, store, rank, world, timeout=10.0, prefix="ssm_peer", poll=0.005):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout, self.prefix, self.poll = float(timeout), prefix, poll
+        self.k = 0
+
+    @classmethod
+    def for_group(cls, timeout=10.0, group=None, prefix="ssm_peer"):
+        """A check over the default process group's store (``group`` only sets rank and size)."""
+        store = dist.distributed_c10d._get_default_store()
+        return cls(store, _rank(group), _world(group), timeout, prefix)
+
+    def _key(self, k, r):
+        return f"{self.prefix}/{k}/{r}"
+
+    def step(self):
+        k = self.k
+        self.k += 1
+        self.store.set(self._key(k, self.rank), b"1")
+        keys = [self._key(k, r) for r in range(self.world)]
+        deadline = time.monotonic() + self.timeout
+        while not self.store.check(keys):
+            if time.monotonic() > deadline:
+                missing = [r for r, key in enumerate(keys) if not self.store.check([key])]
+                if missing:
+                    raise PeerLost(k, missing, self.timeout)
+                break
+            time.sleep(self.poll)
+        if k >= 2:
+            self.store.delete_key(self._key(k - 2, self.rank))
+        return k
+
+
 def _rank(group):
     return dist.get_rank(group) if dist.is_initialized() else 0
 
@@ -219,14 +276,16 @@ class SequenceShardedScanFn(torch.autograd.Function):
     the whole sequence) are all-reduced, and dh0 comes out of the suffix composition on every rank."""
 
     @staticmethod
-    def forward(ctx, x, delta, A, Bm, Cm, h0, D, z, method, group):
+    def forward(ctx, x, delta, A, Bm, Cm, h0, D, z, method, group, peers):
         shard = SequenceShard(x, delta, A, Bm, Cm, method, D, z)
         decay, hend = shard.summary()
+        if peers is not None:
+            peers.step()
         decays, hends = exchange_summaries(decay, hend, group)
         h_in, last = compose_prefix(decays, hends, h0)
         need_bwd = any(ctx.needs_input_grad[:8])
         y, _ = shard.finish(h_in[_rank(group)], save=need_bwd)
-        ctx.shard, ctx.group, ctx.has_h0 = (shard if need_bwd else None), group, h0 is not None
+        ctx.shard, ctx.group, ctx.has_h0, ctx.peers = (shard if need_bwd else None), group, h0 is not None, peers
         return y, last
 
     @staticmethod
@@ -237,6 +296,8 @@ class SequenceShardedScanFn(torch.autograd.Function):
         dl = torch.zeros(shard.shape[0], shard.shape[2], shard.shape[3], dtype=torch.float32, device=shard.dev)
         if dlast is not None:
             dl.copy_(dlast)
+        if ctx.peers is not None:
+            ctx.peers.step()
         if world > 1:
             dist.all_reduce(dl, group=group)
         decay, dstart = shard.adjoint_summary(dy)
@@ -244,18 +305,19 @@ class SequenceShardedScanFn(torch.autograd.Function):
         dl_in, dh0 = compose_suffix(decays, dstarts, dl)
         du, ddelta, dA, dB, dC, _, dD, dz = shard.backward(dy, dl_in[rank])
         reduce_shared_grads([dA, dD], group)        # each rank holds its shard's share of the time sums
-        return du, ddelta, dA, dB, dC, (dh0 if ctx.has_h0 else None), dD, dz, None, None
+        return du, ddelta, dA, dB, dC, (dh0 if ctx.has_h0 else None), dD, dz, None, None, None
 
 
-def sequence_sharded_scan(x, delta, A, Bm, Cm, h0=None, method="zoh", D=None, z=None, group=None):
+def sequence_sharded_scan(x, delta, A, Bm, Cm, h0=None, method="zoh", D=None, z=None, group=None, peers=None):
     """Selective scan of one sequence split over the ranks of ``group`` (differentiable).
 
     This rank holds shard ``rank``: x, delta, z: (B, L_shard, D); Bm, Cm: (B, L_shard, N); A, D,
     h0 are replicated.  Returns (y_shard, last) where last is the final state of the WHOLE
     sequence (on every rank).  Gradients: du, ddelta, dz, dBm, dCm for this shard's rows; dA, dD
-    and dh0 for the whole sequence, identical on every rank."""
+    and dh0 for the whole sequence, identical on every rank.  ``peers`` (a ``PeerCheck``) makes every
+    rank confirm that all others are alive before each exchange, raising ``PeerLost`` otherwise."""
     x2, delta2, A2, Bm2, Cm2, h02, D2, z2 = _prepare(x, delta, A, Bm, Cm, h0, D, z, method)
-    y, last = SequenceShardedScanFn.apply(x2, delta2, A2, Bm2, Cm2, h02, D2, z2, method, group)
+    y, last = SequenceShardedScanFn.apply(x2, delta2, A2, Bm2, Cm2, h02, D2, z2, method, group, peers)
     return y.to(x.dtype), last
 
 

@@ -45,23 +45,27 @@ def s4d_real_A(D, N, dtype=torch.float32):
     return -torch.exp(torch.log(torch.arange(1, N + 1, dtype=torch.float32))).repeat(D, 1).to(dtype)
 
 
-def make_inputs(B, L, D, N, seed=0, dist="config", h0=False, dlast=False, dtype=torch.float32, device="cpu"):
+def make_inputs(B, L, D, N, seed=0, dist="config", h0=False, dlast=False, dtype=torch.float32, device="cpu",
+                draw_on_device=False):
     """Returns a dict of CPU-drawn inputs moved to ``device`` (A, Dskip, h0 stay float32).
 
     Keys: u, delta, A, Bm, Cm, Dskip, z, dy, h0 (or None), dlast (or None).
+    ``draw_on_device`` draws on ``device`` with its own generator (same distributions, different
+    values; for benchmark-sized inputs that would take the CPU tens of seconds to draw).
     """
-    g = torch.Generator().manual_seed(seed)
+    g = torch.Generator(device=device if draw_on_device else "cpu").manual_seed(seed)
+    on = dict(device=device) if draw_on_device else {}
 
     def randn(*s):
-        return torch.randn(*s, generator=g)
+        return torch.randn(*s, generator=g, **on)
 
     u = randn(B, L, D)
     if dist == "config":
         delta = torch.nn.functional.softplus(0.5 * randn(B, L, D) + math.log(math.expm1(0.01)))
-        A = s4d_real_A(D, N)
+        A = s4d_real_A(D, N).to(u.device)
     elif dist == "test":
-        delta = torch.rand(B, L, D, generator=g) * 0.3 + 1e-3
-        A = -torch.rand(D, N, generator=g) * 4 - 0.05
+        delta = torch.rand(B, L, D, generator=g, **on) * 0.3 + 1e-3
+        A = -torch.rand(D, N, generator=g, **on) * 4 - 0.05
     else:
         raise ValueError(dist)
     Bm, Cm = randn(B, L, N), randn(B, L, N)
@@ -87,6 +91,13 @@ def algorithmic_bytes(B, L, D, N, elem_bytes, fused=True, backward=True):
     fwd = (4 if fused else 3) * bld * elem_bytes + 2 * bln * elem_bytes + D * N * 4 + D * 4 + B * D * N * 4
     bwd = (7 if fused else 5) * bld * elem_bytes + 4 * bln * elem_bytes + 2 * D * N * 4 + 2 * D * 4
     return fwd, (bwd if backward else 0)
+
+
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each kernel on each
+# workload, from the ncu captures summarised under profiles/ (the summary named beside each entry
+# gives the command).  bench.py reports it as roofline.traffic; kernels and workloads not listed
+# have not been captured on the current build (traffic null).
+NCU_TRAFFIC = {}
 
 
 def markov_bytes(batch, length, seed=0, order=2, vocab=256, temperature=0.5):

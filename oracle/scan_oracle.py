@@ -7,6 +7,7 @@ It follows the reference (aman078-ai/mamba-ssm-benchmark) step by step:
   discretize            models/scan.py:39-55
   scan_sequential       models/scan.py:70-76
   scan_hillis_steele    models/scan.py:79-98   (with the h0 fold of :79-84)
+  scan_blelloch         models/scan.py:101-135 (Blelloch's work-efficient up/down-sweep scan)
   default_chunk         models/scan.py:138-139
   scan_chunked          models/scan.py:142-165
   channel blocks        models/scan.py:180-190
@@ -69,6 +70,45 @@ def scan_hillis_steele(a, b, h0=None):
     return b
 
 
+def scan_blelloch(a, b, h0=None):
+    """Work-efficient two-sweep scan (Blelloch 1990) of the affine maps h -> a_t h + b_t along dim 1.
+
+    The sequence is padded to a power of two P with identity maps (a = 1, b = 0).  Up-sweep: at
+    stride 2d every node r = 2d k + 2d - 1 becomes "node r - d, then node r" (the total of its
+    subtree).  The root is replaced by the identity; down-sweep: at each stride the left child
+    takes its parent's prefix and the right child becomes "parent's prefix, then the left
+    subtree's total".  Each position then holds the map of all steps before it (an exclusive
+    prefix), so the state after step t is a_t (prefix_t(h0)) + b_t."""
+    Bsz, L = a.shape[:2]
+    rest = tuple(a.shape[2:])
+    P = 1 << max(0, (L - 1).bit_length())
+    pa = torch.cat([a, a.new_ones((Bsz, P - L) + rest)], dim=1)
+    pb = torch.cat([b, b.new_zeros((Bsz, P - L) + rest)], dim=1)
+    d = 1
+    while d < P:                                   # up-sweep
+        r = torch.arange(2 * d - 1, P, 2 * d)
+        left = r - d
+        pb[:, r] = pa[:, r] * pb[:, left] + pb[:, r]
+        pa[:, r] = pa[:, r] * pa[:, left]
+        d *= 2
+    pa[:, P - 1] = 1.0
+    pb[:, P - 1] = 0.0
+    d = P // 2
+    while d >= 1:                                  # down-sweep
+        r = torch.arange(2 * d - 1, P, 2 * d)
+        left = r - d
+        la, lb = pa[:, left].clone(), pb[:, left].clone()
+        pa[:, left], pb[:, left] = pa[:, r], pb[:, r]
+        pb[:, r] = la * pb[:, r] + lb
+        pa[:, r] = la * pa[:, r]
+        d //= 2
+    prev = pb[:, :L] if h0 is None else pb[:, :L] + pa[:, :L] * h0.unsqueeze(1)
+    return a * prev + b
+
+
+SCANS = {"sequential": scan_sequential, "hillis_steele": scan_hillis_steele, "blelloch": scan_blelloch}
+
+
 def default_chunk(L):
     return max(4, 1 << math.ceil(math.log2(max(1.0, math.sqrt(L)))))
 
@@ -104,7 +144,9 @@ def channel_blocks(B, L, D, N, d_block=None):
     return [(i, min(i + d_block, D)) for i in range(0, D, d_block)]
 
 
-def _scan_fn(chunk_size):
+def _scan_fn(chunk_size, name="chunked"):
+    if name != "chunked":
+        return SCANS[name]
     return lambda a, b, h0=None: scan_chunked(a, b, h0, chunk_size)
 
 
@@ -139,8 +181,8 @@ class ChunkedScanFn(torch.autograd.Function):
     through the discretisation analytically."""
 
     @staticmethod
-    def forward(ctx, x, delta, A, Bm, Cm, h0, method, d_block, chunk_size):
-        scan = _scan_fn(chunk_size)
+    def forward(ctx, x, delta, A, Bm, Cm, h0, method, d_block, chunk_size, scan_name="chunked"):
+        scan = _scan_fn(chunk_size, scan_name)
         Bsz, L, D = x.shape
         N = A.shape[1]
         y = torch.empty_like(x)
@@ -151,14 +193,14 @@ class ChunkedScanFn(torch.autograd.Function):
             y[..., i:j] = torch.einsum("bldn,bln->bld", h, Cm)
             last[:, i:j] = h[:, -1]
         ctx.save_for_backward(x, delta, A, Bm, Cm, h0)
-        ctx.cfg = (method, d_block, chunk_size)
+        ctx.cfg = (method, d_block, chunk_size, scan_name)
         return y, last
 
     @staticmethod
     def backward(ctx, dy, dlast):
         x, delta, A, Bm, Cm, h0 = ctx.saved_tensors
-        method, d_block, chunk_size = ctx.cfg
-        scan = _scan_fn(chunk_size)
+        method, d_block, chunk_size, scan_name = ctx.cfg
+        scan = _scan_fn(chunk_size, scan_name)
         Bsz, L, D = x.shape
         N = A.shape[1]
         grads = dict(x=torch.empty_like(x), delta=torch.empty_like(delta), A=torch.empty_like(A),
@@ -184,7 +226,7 @@ class ChunkedScanFn(torch.autograd.Function):
             grads["x"][..., i:j] = torch.einsum("bldn,bln->bld", dhc, Bm)
             if hb0 is not None:
                 grads["h0"][:, i:j] = dh[:, 0] * a[:, 0]
-        return (grads["x"], grads["delta"], grads["A"], grads["B"], grads["C"], grads["h0"], None, None, None)
+        return (grads["x"], grads["delta"], grads["A"], grads["B"], grads["C"], grads["h0"], None, None, None, None)
 
 
 def selective_scan_loop(x, delta, A, Bm, Cm, h0=None, method="zoh"):
@@ -207,10 +249,10 @@ def selective_scan(x, delta, A, Bm, Cm, h0=None, method="zoh", scan="chunked", d
         args = [None if t is None else t.to(ct) for t in (x, delta, A, Bm, Cm, h0)]
         if scan == "reference":
             y, last = selective_scan_loop(*args, method=method)
-        elif scan == "chunked":
-            y, last = ChunkedScanFn.apply(*args, method, d_block, chunk_size)
+        elif scan == "chunked" or scan in SCANS:
+            y, last = ChunkedScanFn.apply(*args, method, d_block, chunk_size, scan)
         else:
-            raise ValueError(f"oracle implements scan='chunked' and 'reference', not {scan!r}")
+            raise ValueError(f"oracle implements scan='chunked', {sorted(SCANS)} and 'reference', not {scan!r}")
     return y.to(dtype), last
 
 

@@ -12,6 +12,9 @@ seeded inputs and the reference's outputs:
                                    (the autograd ground truth), same cotangents
   chunked_scan.npz                 models/scan.py:scan_chunked on random (a, b) for several
                                    chunk sizes, with and without h0
+  scans.npz                        models/scan.py:scan_sequential, scan_hillis_steele and
+                                   scan_blelloch on random (a, b), L = 50 and L = 64, +- h0, and
+                                   selective_scan with scan="blelloch" (y, last, gradients)
   fused_cfg.npz                    config-distribution inputs through selective_scan + the
                                    mixer gate (y + x*D)*silu(z) (models/mamba.py:124)
   decode.npz                       the inline decode step of models/mamba.py:113-118
@@ -80,6 +83,8 @@ def main(argv=None):
         bench_inputs()
     if args.only == "lm_small" or args.only is None:
         lm_small()
+    if args.only == "scans" or args.only is None:
+        scans(ref)
     if args.only is not None:
         return
 
@@ -130,6 +135,24 @@ def main(argv=None):
         res[f"state_{method}"] = h
     _save("decode.npz", **{k: _np(v) for k, v in res.items()})
     print("wrote", len([f for f in os.listdir(HERE) if f.endswith(".npz")]), "fixtures to", HERE)
+
+
+def scans(ref):
+    """The reference's alternative scan algorithms (models/scan.py:70-135) on random affine maps."""
+    g = torch.Generator().manual_seed(17)
+    res = {}
+    for L in (50, 64):
+        a = torch.rand(2, L, 3, 4, generator=g, dtype=torch.float64) * 0.9 + 0.05
+        b = torch.randn(2, L, 3, 4, generator=g, dtype=torch.float64)
+        h0 = torch.randn(2, 3, 4, generator=g, dtype=torch.float64)
+        res[f"a{L}"], res[f"b{L}"], res[f"h0_{L}"] = _np(a), _np(b), _np(h0)
+        for name in ("sequential", "hillis_steele", "blelloch"):
+            fn = getattr(ref, f"scan_{name}")
+            res[f"{name}{L}"] = _np(fn(a, b))
+            res[f"{name}{L}_h0"] = _np(fn(a, b, h0))
+    arr = scan_case(ref.selective_scan, (2, 37, 50, 16), "zoh", True, torch.float32, "blelloch", seed=77)
+    res.update({f"sel_{k}": v for k, v in arr.items()})
+    _save("scans.npz", **res)
 
 
 def lm_small():

@@ -79,8 +79,11 @@ def test_python_api_rejects_like_the_reference():
         selective_scan_triton(x, x, A, Bm, Bm, method="rk4")
     with pytest.raises(ValueError, match="power of two"):
         selective_scan_triton(x, x, -torch.ones(8, 12), torch.zeros(1, 4, 12), torch.zeros(1, 4, 12))
-    with pytest.raises(ValueError, match="does not ship"):
-        selective_scan(x, x, A, Bm, Bm, scan="chunked")
+    with pytest.raises(ValueError, match="unknown scan"):
+        selective_scan(x, x, A, Bm, Bm, scan="fft")
+    for name in ("chunked", "reference", "blelloch"):     # the reference's names: no CPU path here
+        with pytest.raises(RuntimeError, match="CUDA"):
+            selective_scan(x, x, A, Bm, Bm, scan=name)
     with pytest.raises(RuntimeError, match="CUDA"):
         selective_scan_triton(x, x, A, Bm, Bm)
     for shape in ((1, 0, 8), (0, 4, 8)):

@@ -57,6 +57,28 @@ def test_oracle_two_level_scan_matches_reference():
     torch.testing.assert_close(O.scan_sequential(case["a"], case["b"], case["h0"]), case["h_c1_h0"])
 
 
+@pytest.mark.parametrize("name", ["sequential", "hillis_steele", "blelloch"])
+def test_oracle_alternative_scans_match_reference(name):
+    """models/scan.py:70-135 on random affine maps (float64), L = 50 (padded inside Blelloch) and
+    L = 64, with and without h0."""
+    case = load_golden("scans.npz")
+    fn = O.SCANS[name]
+    for L in (50, 64):
+        a, b, h0 = case[f"a{L}"], case[f"b{L}"], case[f"h0_{L}"]
+        torch.testing.assert_close(fn(a, b), case[f"{name}{L}"], rtol=1e-12, atol=1e-12)
+        torch.testing.assert_close(fn(a, b, h0), case[f"{name}{L}_h0"], rtol=1e-12, atol=1e-12)
+
+
+def test_oracle_blelloch_selective_scan_matches_reference():
+    """selective_scan(scan="blelloch") in float32 with its recomputing backward."""
+    case = {k[4:]: v for k, v in load_golden("scans.npz").items() if k.startswith("sel_")}
+    y, last, grads = _run(case, "zoh", torch.float32, "blelloch")
+    torch.testing.assert_close(y, case["y"], rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(last, case["last"], rtol=1e-5, atol=1e-5)
+    for n, g in zip(("du", "ddelta", "dA", "dBm", "dCm", "dh0"), grads):
+        assert O.normwise_error(g, case[n]) < 1e-5, n
+
+
 def test_oracle_fused_gate_matches_reference():
     case = load_golden("fused_cfg.npz")
     out, last = O.selective_scan_fused(case["u"], case["delta"], case["A"], case["Bm"], case["Cm"],

@@ -22,8 +22,9 @@ DEV = "cuda"
 def _forward(ins, B, L, D, N):
     """Runs ssm_scan_fwd for training: returns (chunk_states, ygate)."""
     lib = nat.lib()
-    y = torch.empty(B, L, D, device=DEV)
-    yg = torch.empty(B, L, D, device=DEV)
+    dt = ins["u"].dtype
+    y = torch.empty(B, L, D, device=DEV, dtype=dt)
+    yg = torch.empty(B, L, D, device=DEV, dtype=dt)
     last = torch.empty(B, D, N, device=DEV)
     cs = torch.empty(B, -(-L // 16), D, N, device=DEV)
     wsb = nat.fwd_workspace_bytes(B, L, D, N)
@@ -36,12 +37,17 @@ def _forward(ins, B, L, D, N):
     return cs, yg
 
 
-def _backward(ins, cs, yg, B, L, D, N, noalloc):
+def _outputs(B, L, D, N, dt):
+    a = dict(device=DEV, dtype=dt)
+    return dict(du=torch.empty(B, L, D, **a), ddelta=torch.empty(B, L, D, **a),
+                dA=torch.empty(D, N, device=DEV), dB=torch.empty(B, L, N, **a),
+                dC=torch.empty(B, L, N, **a), dD=torch.empty(D, device=DEV),
+                dz=torch.empty(B, L, D, **a), dh0=torch.empty(B, D, N, device=DEV))
+
+
+def _backward(ins, cs, yg, B, L, D, N, noalloc, out=None):
     lib = nat.lib()
-    out = dict(du=torch.empty(B, L, D, device=DEV), ddelta=torch.empty(B, L, D, device=DEV),
-               dA=torch.empty(D, N, device=DEV), dB=torch.empty(B, L, N, device=DEV),
-               dC=torch.empty(B, L, N, device=DEV), dD=torch.empty(D, device=DEV),
-               dz=torch.empty(B, L, D, device=DEV), dh0=torch.empty(B, D, N, device=DEV))
+    out = out if out is not None else _outputs(B, L, D, N, ins["u"].dtype)
     common = (B, L, D, N, 0, nat.view3(ins["u"]), nat.view3(ins["delta"]), nat.ptr(ins["A"]), nat.view3(ins["Bm"]),
               nat.view3(ins["Cm"]), nat.ptr(ins["Dskip"]), nat.view3(ins["z"]), nat.ptr(ins["h0"]), nat.ptr(cs),
               nat.view3(yg), nat.view3(ins["dy"]), nat.ptr(ins["dlast"]), nat.view3(out["du"]),
@@ -59,21 +65,22 @@ def _backward(ins, cs, yg, B, L, D, N, noalloc):
     return out
 
 
-@pytest.mark.parametrize("shape", [(2, 100, 64, 16), (16, 512, 512, 16), (3, 37, 50, 8)],
-                         ids=lambda s: "x".join(map(str, s)))
-def test_noalloc_backward_matches_workspace_backward_twice(shape):
+@pytest.mark.parametrize("shape,dtype", [((2, 100, 64, 16), torch.float32), ((16, 512, 512, 16), torch.float32),
+                                         ((3, 37, 50, 8), torch.float32), ((2, 300, 96, 16), torch.bfloat16)],
+                         ids=["2x100x64x16", "16x512x512x16", "3x37x50x8", "2x300x96x16-bf16"])
+def test_noalloc_backward_matches_workspace_backward_twice(shape, dtype):
     B, L, D, N = shape
     assert nat.bwd_workspace_bytes(B, L, D, N) <= 32 << 20
     results = []
     for seed in (1, 2):                      # two calls in a row on different inputs
-        ins = make_inputs(B, L, D, N, seed=seed, dist="config", h0=True, dlast=True)
+        ins = make_inputs(B, L, D, N, seed=seed, dist="config", h0=True, dlast=True, dtype=dtype)
         ins = {k: (v.to(DEV) if v is not None else None) for k, v in ins.items()}
         cs, yg = _forward(ins, B, L, D, N)
         ref = _backward(ins, cs, yg, B, L, D, N, noalloc=False)
         got = _backward(ins, cs, yg, B, L, D, N, noalloc=True)
         for k in ref:
-            assert torch.isfinite(got[k]).all(), k
-            assert O.normwise_error(got[k], ref[k]) <= H.GRAD_TOL, k
+            assert torch.isfinite(got[k].float()).all(), k
+            assert O.normwise_error(got[k].float(), ref[k].float()) <= H.GRAD_TOL, k
         results.append(got)
     # the second call did not leave the first call's values behind
     assert not torch.equal(results[0]["dB"], results[1]["dB"])
@@ -88,3 +95,24 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
                                         None, v, v, None, v, None, None)
     assert rc == nat.SSM_ERR_WORKSPACE
     assert b"built-in scratch" in nat.lib().ssm_last_error_message()
+
+
+def test_noalloc_call_allocates_no_device_memory():
+    """With its inputs and outputs in place, the call leaves the device's free memory and torch's
+    allocator untouched: it uses only the built-in scratch."""
+    B, L, D, N = 4, 256, 128, 16
+    ins = make_inputs(B, L, D, N, seed=3, dist="config", h0=True, dlast=True)
+    ins = {k: (v.to(DEV) if v is not None else None) for k, v in ins.items()}
+    cs, yg = _forward(ins, B, L, D, N)
+    out = _outputs(B, L, D, N, torch.float32)
+    _backward(ins, cs, yg, B, L, D, N, noalloc=True, out=out)       # first call on this device
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    held0, peak0 = torch.cuda.memory_allocated(), torch.cuda.max_memory_allocated()
+    for _ in range(3):
+        _backward(ins, cs, yg, B, L, D, N, noalloc=True, out=out)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert torch.cuda.memory_allocated() == held0 and torch.cuda.max_memory_allocated() == peak0
+    assert nat.read_device_error() == 0
