@@ -119,6 +119,14 @@ def test_sequence_shards_backward_single_gpu(shards, method):
     assert O.normwise_error(last, last1) < 1e-5
     for k in keys:
         assert O.normwise_error(got[k], want[k]) < 1e-4, k
+    # and the stitched gradients against the oracle (models/scan.py:219-255 restated) directly
+    cpu = {k: ins[k].clone().requires_grad_() for k in keys}
+    yr, lr = O.selective_scan_fused(cpu["u"], cpu["delta"], cpu["A"], cpu["Bm"], cpu["Cm"], h0=cpu["h0"],
+                                    method=method, Dskip=cpu["Dskip"], z=cpu["z"])
+    ref = dict(zip(keys, torch.autograd.grad((yr, lr), [cpu[k] for k in keys], (ins["dy"], ins["dlast"]))))
+    assert O.normwise_error(torch.cat(ys, 1), yr) < 1e-4
+    for k in keys:
+        assert O.normwise_error(got[k], ref[k]) < 1e-3, k
 
 
 def test_sequence_sharded_scan_without_process_group():
