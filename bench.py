@@ -66,7 +66,20 @@ def parse(argv=None):
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sub", action="store_true", help="headline only (no sub-records)")
+    ap.add_argument("--shape", default=None,
+                    help="B,L,D overriding the workload's shape (a smaller case of it, for profiling)")
     return ap.parse_args(argv)
+
+
+def workload_config(args, cfg_id):
+    """CONFIGS[cfg_id], with --shape applied when it names this workload (the headline)."""
+    import dataclasses
+    from mamba_ssm_benchmark_b200.workloads import CONFIGS
+    cfg = CONFIGS[cfg_id]
+    if args.shape and cfg_id == args.config:
+        B, L, D = (int(v) for v in args.shape.split(","))
+        cfg = dataclasses.replace(cfg, B=B, L=L, D=D, name=f"{cfg.name}_shape{B}x{L}x{D}")
+    return cfg
 
 
 def dist_env():
@@ -614,8 +627,8 @@ def channel_record(args, cfg_id, scaling, rank, world, device, sets, cpu):
     """Configs 1 (weak: every rank a full D-channel layer shard) and 3 (strong: D split over the
     ranks).  Returns the record (meaningful on rank 0)."""
     from mamba_ssm_benchmark_b200 import sharding
-    from mamba_ssm_benchmark_b200.workloads import CONFIGS, algorithmic_bytes
-    cfg = CONFIGS[cfg_id]
+    from mamba_ssm_benchmark_b200.workloads import algorithmic_bytes
+    cfg = workload_config(args, cfg_id)
     if scaling == "strong":
         lo, hi = sharding.shard_range(cfg.D, world, rank)
     else:
@@ -670,8 +683,8 @@ def sequence_record(args, cfg_id, rank, world, device, cpu):
     (which splits it into segments itself)."""
     from mamba_ssm_benchmark_b200 import _native as nat
     from mamba_ssm_benchmark_b200 import selective_scan_fused, sharding
-    from mamba_ssm_benchmark_b200.workloads import CONFIGS, algorithmic_bytes, make_inputs
-    cfg = CONFIGS[cfg_id]
+    from mamba_ssm_benchmark_b200.workloads import algorithmic_bytes, make_inputs
+    cfg = workload_config(args, cfg_id)
     lo, hi = sharding.shard_range(cfg.L, world, rank)
     Ls = hi - lo
     B, D, N = cfg.B, cfg.D, cfg.N
@@ -918,8 +931,7 @@ def run_lm(args, rank, world, device):
 
 def main():
     args = parse()
-    from mamba_ssm_benchmark_b200.workloads import CONFIGS
-    cfg = CONFIGS.get(args.config)
+    cfg = workload_config(args, args.config) if args.config != 4 else None
     if args.impl == "reference":
         if cfg is None:
             if dist_env()[0] == 0:
