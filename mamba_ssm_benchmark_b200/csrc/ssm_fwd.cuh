@@ -50,7 +50,11 @@ struct FwdSmem {
   static constexpr int STAGE = 3 * ACT + 2 * BC;
   static constexpr int OFF_BAR = NSTAGE * STAGE;
   static constexpr int OFF_SDT = OFF_BAR + NSTAGE * 8;   // dt_softplus: the box's activated deltas (fp32)
-  static constexpr int BYTES = OFF_SDT + TC * BXC * 4;
+  // bf16: the current box's B and C converted to fp32 once (a lane would otherwise unpack eight bf16
+  // values per step); fp32 reads the staged box directly
+  static constexpr int OFF_BCF = (OFF_SDT + TC * BXC * 4 + 15) / 16 * 16;
+  static constexpr int BCF = (E == 2) ? 2 * TB * N * 4 : 0;
+  static constexpr int BYTES = OFF_BCF + BCF;
   static_assert(ACT % 128 == 0 && BC % 128 == 0, "TMA boxes must stay 128-byte aligned");
 };
 
@@ -252,13 +256,35 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
         fwd_warp_load<S, N, T, MODE>(p, st, x0, box_t0(q), b);
         __syncwarp();
       }
+      if constexpr (sizeof(T) == 2) {   // the box's B (and C) as fp32: 8 values per 16-byte load
+        constexpr int NV = S::TB * N / 8;
+        float4* const dst = reinterpret_cast<float4*>(smem + S::OFF_BCF);
+        const uint4* const srcB = reinterpret_cast<const uint4*>(st + S::OFF_B);
+        const uint4* const srcC = reinterpret_cast<const uint4*>(st + S::OFF_C);
+        auto widen = [&](const uint4* src, float4* out, int v) {
+          const uint4 w = src[v];
+          out[2 * v] = make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u),
+                                   __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u));
+          out[2 * v + 1] = make_float4(__uint_as_float(w.z << 16), __uint_as_float(w.z & 0xffff0000u),
+                                       __uint_as_float(w.w << 16), __uint_as_float(w.w & 0xffff0000u));
+        };
+#pragma unroll
+        for (int v = lane; v < NV; v += 32) {
+          widen(srcB, dst, v);
+          if (MODE == kModeMain) widen(srcC, dst + NV * 2, v);
+        }
+        __syncwarp();
+      }
     }
     // this tile's rows of the box
     const T* __restrict__ Xs = reinterpret_cast<const T*>(st + S::OFF_U) + sub * TC * BXC;
     const T* __restrict__ DLs = reinterpret_cast<const T*>(st + S::OFF_DT) + sub * TC * BXC;
     const T* __restrict__ Zs = reinterpret_cast<const T*>(st + S::OFF_Z) + sub * TC * BXC;
-    const T* __restrict__ Bs = reinterpret_cast<const T*>(st + S::OFF_B) + sub * TC * N;
-    const T* __restrict__ Cs = reinterpret_cast<const T*>(st + S::OFF_C) + sub * TC * N;
+    // B and C of this tile's rows as fp32 (bf16: the widened copies of the box)
+    const float* __restrict__ Bs = (sizeof(T) == 2 ? reinterpret_cast<const float*>(smem + S::OFF_BCF)
+                                                   : reinterpret_cast<const float*>(st + S::OFF_B)) + sub * TC * N;
+    const float* __restrict__ Cs = (sizeof(T) == 2 ? reinterpret_cast<const float*>(smem + S::OFF_BCF) + S::TB * N
+                                                   : reinterpret_cast<const float*>(st + S::OFF_C)) + sub * TC * N;
 
     if (MODE == kModeMain && p.chunk_states != nullptr && dvalid)   // state entering chunk t0 / 16
       storep<G>(p.chunk_states + (((size_t)b * p.nchunks + t0 / TC) * p.D + d) * N + nbase, h);
