@@ -11,9 +11,9 @@ It follows the reference (aman078-ai/mamba-ssm-benchmark) step by step:
   default_chunk         models/scan.py:138-139
   scan_chunked          models/scan.py:142-165
   channel blocks        models/scan.py:180-190
-  ChunkedScanFn         models/scan.py:193-255 (forward + recomputing backward; the
-                        backward's chain rule through discretize, which the reference takes
-                        with autograd at :249, is written out analytically here)
+  ChunkedScanFn         models/scan.py:193-255 (forward + recomputing backward, driven by
+                        any of the scans; the chain rule through discretize by autograd,
+                        as at :249)
   selective_scan_loop   models/scan.py:264-274 (autograd through a time loop: ground truth)
   selective_scan        models/scan.py:277-299 (dtype promotion, autocast off)
   gate                  models/mamba.py:124
@@ -127,14 +127,14 @@ def scan_chunked(a, b, h0=None, chunk_size=None):
     b = b.reshape((Bsz, nc, C) + rest)
     local = torch.empty_like(b)
     local[:, :, 0] = b[:, :, 0]
-    for t in range(1, C):
-        local[:, :, t] = b[:, :, t] + a[:, :, t] * local[:, :, t - 1]
+    for t in range(1, C):                          # fused multiply-add per step, into the output
+        torch.addcmul(b[:, :, t], a[:, :, t], local[:, :, t - 1], out=local[:, :, t])
     decay = torch.cumprod(a, dim=2)
     ends = scan_hillis_steele(decay[:, :, -1], local[:, :, -1], h0)
     first = torch.zeros_like(ends[:, :1]) if h0 is None else h0[:, None]
     carry = torch.cat([first, ends[:, :-1]], dim=1)
-    h = local + decay * carry[:, :, None]
-    return h.reshape((Bsz, nc * C) + rest)[:, :L]
+    local.addcmul_(decay, carry[:, :, None])       # fix-up in place
+    return local.reshape((Bsz, nc * C) + rest)[:, :L]
 
 
 def channel_blocks(B, L, D, N, d_block=None):
@@ -150,35 +150,11 @@ def _scan_fn(chunk_size, name="chunked"):
     return lambda a, b, h0=None: scan_chunked(a, b, h0, chunk_size)
 
 
-def discretize_with_partials(delta, A, Bm, x, method="zoh"):
-    """a, b of discretize() plus the partials the backward needs, all (B, L, D, N):
-
-    coef = db/d(B x);  a_d, b_d = da/ddelta, db/ddelta;  a_A, b_A = da/dA, db/dA.
-    ZOH's db/dA uses A db/dA = delta db/ddelta - coef Bx, the exact form of
-    (z e^z - expm1 z) / z^2 that needs no small-z branch.
-    """
-    z = delta[..., None] * A
-    bx = x[..., None] * Bm[:, :, None, :]
-    dt = delta[..., None]
-    if method == "zoh":
-        a = torch.exp(z)
-        coef = torch.expm1(z) / A
-        return a, coef * bx, coef, A * a, a * bx, dt * a, (dt * a - coef) * bx / A
-    if method == "euler":
-        a = torch.exp(z)
-        return a, dt * bx, dt.expand_as(z), A * a, bx, dt * a, torch.zeros_like(z)
-    if method == "bilinear":
-        w = 1.0 / (1.0 - 0.5 * z)
-        w2 = w * w
-        return (1.0 + 0.5 * z) * w, dt * w * bx, dt * w, A * w2, w2 * bx, dt * w2, 0.5 * dt * dt * w2 * bx
-    raise ValueError(f"unknown discretization {method!r}")
-
-
 class ChunkedScanFn(torch.autograd.Function):
     """Memory-bounded selective scan: saves only the inputs; the backward recomputes the states
-    of one channel block at a time with the chunked scan, runs the adjoint recurrence
-    dh_t = g_t + a_{t+1} dh_{t+1} as a reversed chunked scan, and applies the chain rule
-    through the discretisation analytically."""
+    of one channel block at a time with the chosen scan, runs the adjoint recurrence
+    dh_t = g_t + a_{t+1} dh_{t+1} as a reversed scan, and takes the chain rule through the
+    discretisation with autograd on (a, b) = discretize(...) (models/scan.py:219-255)."""
 
     @staticmethod
     def forward(ctx, x, delta, A, Bm, Cm, h0, method, d_block, chunk_size, scan_name="chunked"):
@@ -207,25 +183,30 @@ class ChunkedScanFn(torch.autograd.Function):
                      B=torch.zeros_like(Bm), C=torch.zeros_like(Cm),
                      h0=None if h0 is None else torch.empty_like(h0))
         for i, j in channel_blocks(Bsz, L, D, N, d_block):
-            xb, hb0 = x[..., i:j], (None if h0 is None else h0[:, i:j])
-            a, b, coef, a_d, b_d, a_A, b_A = discretize_with_partials(delta[..., i:j], A[i:j], Bm, xb, method)
-            h = scan(a, b, hb0)
-            dyb = dy[..., i:j]
-            grads["C"] += torch.einsum("bld,bldn->bln", dyb, h)
-            g = dyb[..., None] * Cm[:, :, None, :]
-            if dlast is not None:
-                g[:, -1] += dlast[:, i:j]
-            a_shift = torch.cat([a[:, 1:], torch.ones_like(a[:, :1])], dim=1)
-            dh = scan(a_shift.flip(1), g.flip(1)).flip(1)
-            start = torch.zeros_like(h[:, :1]) if hb0 is None else hb0[:, None]
-            hp = torch.cat([start, h[:, :-1]], dim=1)
-            grads["delta"][..., i:j] = (dh * (hp * a_d + b_d)).sum(-1)
-            grads["A"][i:j] = (dh * (hp * a_A + b_A)).sum((0, 1))
-            dhc = dh * coef
-            grads["B"] += torch.einsum("bldn,bld->bln", dhc, xb)
-            grads["x"][..., i:j] = torch.einsum("bldn,bln->bld", dhc, Bm)
-            if hb0 is not None:
-                grads["h0"][:, i:j] = dh[:, 0] * a[:, 0]
+            hb0 = None if h0 is None else h0[:, i:j]
+            with torch.enable_grad():
+                leaves = [t.detach().requires_grad_() for t in (delta[..., i:j], A[i:j], Bm, x[..., i:j])]
+                a, b = discretize(leaves[0], leaves[1], leaves[2], leaves[3], method)
+            with torch.no_grad():
+                ad = a.detach()
+                h = scan(ad, b.detach(), hb0)
+                dyb = dy[..., i:j]
+                grads["C"] += torch.einsum("bld,bldn->bln", dyb, h)
+                g = dyb[..., None] * Cm[:, :, None, :]
+                if dlast is not None:
+                    g[:, -1] += dlast[:, i:j]
+                a_shift = torch.cat([ad[:, 1:], torch.ones_like(ad[:, :1])], dim=1)
+                dh = scan(a_shift.flip(1), g.flip(1)).flip(1)
+                start = torch.zeros_like(h[:, :1]) if hb0 is None else hb0[:, None]
+                da = dh * torch.cat([start, h[:, :-1]], dim=1)       # d/da of a_t h_{t-1}
+                if hb0 is not None:
+                    grads["h0"][:, i:j] = dh[:, 0] * ad[:, 0]
+                del h, g, a_shift
+            g_delta, g_A, g_B, g_x = torch.autograd.grad((a, b), leaves, (da, dh))
+            grads["delta"][..., i:j] = g_delta
+            grads["A"][i:j] = g_A
+            grads["B"] += g_B
+            grads["x"][..., i:j] = g_x
         return (grads["x"], grads["delta"], grads["A"], grads["B"], grads["C"], grads["h0"], None, None, None, None)
 
 
