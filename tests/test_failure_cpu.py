@@ -56,8 +56,10 @@ def _worker(rank, port, out_dir, scenario):
             if scenario == "late" and rank == 2 and step == 1:
                 time.sleep(0.7)                       # arrives late, within the check's timeout
             if scenario == "leaves" and rank == 2 and step == 1:
-                _report(out_dir, rank, left_at=step)
-                return                                # leaves between steps, nothing in flight
+                _report(out_dir, rank, left_at=step)  # stops taking part between steps, nothing in
+                time.sleep(3.0)                       # flight; its process ends after the others'
+                return                                # check has run out (an exit in the middle can
+                                                      # also surface as a reset gloo connection)
             if scenario == "skips_collective" and rank == 2 and step == 1:
                 peers.step()                          # passes the check, then never joins the exchange
                 time.sleep(8.0)
@@ -74,7 +76,13 @@ def _worker(rank, port, out_dir, scenario):
         _report(out_dir, rank, collective_error=str(e)[:200], elapsed=time.monotonic() - t0)
     finally:
         if not (scenario in ("leaves", "skips_collective") and rank == 2):
-            os._exit(0)                               # skip teardown handshakes with a departed rank
+            # rank 0's process hosts the store the others may still be polling: every rank waits
+            # (bounded) until all have reported, then ends without teardown handshakes
+            deadline = time.monotonic() + 15.0
+            while time.monotonic() < deadline and not all(
+                    os.path.exists(os.path.join(out_dir, f"rank{r}.json")) for r in range(WORLD)):
+                time.sleep(0.05)
+            os._exit(0)
 
 
 def _run(scenario, tmp_path):
