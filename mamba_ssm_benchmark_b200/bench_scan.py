@@ -78,24 +78,35 @@ def time_ms(fn, warmup=2, min_repeats=3, max_repeats=20, budget_ms=500.0):
     return statistics.median(times), q[0], q[2]
 
 
-def peak_mb(fn):
-    torch.cuda.synchronize()
-    torch.cuda.empty_cache()
-    base = torch.cuda.memory_allocated()
-    torch.cuda.reset_peak_memory_stats()
-    fn()
-    torch.cuda.synchronize()
-    return (torch.cuda.max_memory_allocated() - base) / 2**20
+class DevicePeak:
+    """Context manager: the most device memory (MiB) allocated inside the block above what was held
+    when it was entered."""
+
+    def __enter__(self):
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        self.held = torch.cuda.memory_allocated()
+        torch.cuda.reset_peak_memory_stats()
+        self.mib = None
+        return self
+
+    def __exit__(self, *exc):
+        torch.cuda.synchronize()
+        self.mib = (torch.cuda.max_memory_allocated() - self.held) / 2**20
+        return False
 
 
 def measure(fn, **kw):
+    """One record of the result format: one untimed call under the memory probe, then the timed
+    repeats; an out-of-memory error anywhere turns the record into {"oom": true}."""
     try:
-        mem = peak_mb(fn)
+        with DevicePeak() as peak:
+            fn()
         ms, q25, q75 = time_ms(fn, **kw)
-        return {"ms": ms, "q25": q25, "q75": q75, "peak_mb": mem}
     except torch.OutOfMemoryError:
         torch.cuda.empty_cache()
         return {"oom": True}
+    return {"ms": ms, "q25": q25, "q75": q75, "peak_mb": peak.mib}
 
 
 def csv_rows(results):
