@@ -290,8 +290,8 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
     const float zz = to_f32(Zs[e]);
     const float sg = sigmoid(zz);
     const float dys = p.has_z ? dyv * zz * sg : dyv;
-    if (live && p.has_z && t < p.L && dg < p.D)   // a warp stores one 32-channel row
-      dz_out[(long long)t * p.dz.sl + dg] = from_f32<T>(dyv * to_f32(YGs[e]) * sg * fmaf(zz, 1.0f - sg, 1.0f));
+    st_pred(dz_out + (long long)t * p.dz.sl + dg, from_f32<T>(dyv * to_f32(YGs[e]) * sg * fmaf(zz, 1.0f - sg, 1.0f)),
+            live && p.has_z && t < p.L && dg < p.D);   // a warp stores one 32-channel row
     dDacc = live ? fmaf(dys, uu, dDacc) : dDacc;   // thread tid always sees channel tid % 32
     float dtv = to_f32(DLs[e]), sgd = 0.0f;
     if (p.dt_softplus) {                  // rows past L keep delta = 0 (identity steps)
@@ -622,7 +622,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kerne
 #pragma unroll
         for (int w = 0; w < NW; ++w) sum += SRED[(j * NW + w) * 2 * N + v];
         const int t = t0 + j;
-        if (t < p.L) p.part_bc[(((size_t)b * p.ndt + dtile) * p.L + t) * 2 * N + v] = sum;
+        st_pred(p.part_bc + (((size_t)b * p.ndt + dtile) * p.L + t) * 2 * N + v, sum, t < p.L);
       }
 
       if (p.use_tma && tid == 0) {        // the stage just consumed takes chunk nx

@@ -222,8 +222,8 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
       // the gate as a select and predicated stores: no branch inside the step loop this runs in
       const float yo = p.has_z ? yv * (zz[i] * sigmoid(zz[i])) : yv;
       const bool ok = tb >= 0 && dvalid && t < p.L;
-      if (ok && p.save_ygate) ygout[(long long)t * p.yg.sl] = from_f32<T>(yv);
-      if (ok) yout[(long long)t * p.y.sl] = from_f32<T>(yo);
+      st_pred(ygout + (long long)t * p.yg.sl, from_f32<T>(yv), ok && p.save_ygate);
+      st_pred(yout + (long long)t * p.y.sl, from_f32<T>(yo), ok);
     }
   };
   // the previous tile's outputs wait here and are emitted from inside the next tile's step loop,
