@@ -16,7 +16,8 @@
 //       value the reverse pass needs (ZOH: rho = expm1(delta A) / A - delta, Euler: a, bilinear:
 //       1 / (1 - delta A / 2)) -- in a thread-private shared-memory slot;
 //   (4) runs the reverse adjoint through those registers, reading the coefficients back instead
-//       of re-evaluating exponentials (ZOH: coef = delta + rho, a = 1 + A coef).
+//       of re-evaluating exponentials (ZOH: coef = delta + rho, a = 1 + A coef); the bf16 N = 16
+//       layout keeps no cache and re-evaluates them, which fits a third CTA on every SM.
 // Both passes fetch step j+-1's inputs while step j computes, and step j's dB|dC reduction is
 // issued after step j-1's arithmetic, so shared-memory and shuffle latency overlap work.
 // du and ddelta go through padded shared tiles (two sets, stored coalesced at the end of each
@@ -58,6 +59,11 @@ struct BwdSmem {
   using Gm = Geo<N, G>;
   static constexpr int TC = Gm::TC, DT = Gm::DT;
   static constexpr int NSTAGE = 2;
+  // bf16 at N = 16 trades the coefficient cache for a third CTA per SM (168 registers, no cache:
+  // the reverse pass re-evaluates the coefficients).  With the large grids of bf16 layers (config
+  // 3: 1280 CTAs) the extra warps win: 9.53 -> 9.21 ms per backward at config 3, one B200.  fp32
+  // at config 1 (256 CTAs, under two per SM) keeps the cache.
+  static constexpr bool TRIO = N == 16 && G == 4 && sizeof(T) == 2;
   static constexpr int ACT = TC * DT * (int)sizeof(T);
   static constexpr int BC = TC * N * (int)sizeof(T);
   static constexpr int OFF_U = 0, OFF_DT = ACT, OFF_Z = 2 * ACT, OFF_DY = 3 * ACT, OFF_YG = 4 * ACT,
@@ -79,17 +85,20 @@ struct BwdSmem {
   static constexpr int OUT = ((TC * OP * (int)sizeof(T)) + 127) / 128 * 128;
   static constexpr int NOUT = 2;
   // the recompute pass's per-step coefficients: TC steps x NT threads x G values (thread-private);
-  // layouts where they do not fit (N = 64: 128 KB) re-evaluate them in the reverse pass instead
+  // layouts where they do not fit (N = 64: 128 KB), and the three-CTA layout, re-evaluate them in
+  // the reverse pass instead
   static constexpr int CFB_FULL = TC * Gm::NT * G * 4;
   static constexpr int BASE = NSTAGE * STAGE + TC * Gm::NW * 2 * N * 4 + Gm::NT * 4 + NSTAGE * 8 + NOUT * 2 * OUT;
-  static constexpr bool CACHE = BASE + CFB_FULL + SUDB + 2 * BPB <= 227 * 1024;
+  static constexpr bool CACHE = !TRIO && BASE + CFB_FULL + SUDB + 2 * BPB <= 227 * 1024;
   static constexpr int CFB = CACHE ? CFB_FULL : 0;
   static constexpr int FIXED = BASE + CFB;
   // bytes with gate products GA chunks ahead: GA + 1 product buffers
   static constexpr int bytes_for(int ga) { return FIXED + (ga + 1) * (SUDB + 2 * BPB); }
   // per-CTA budget that keeps the CTAs per SM the register file allows (256 threads' worth of
-  // registers at most per 128 threads, G = 2 launches capped at two CTAs per SM)
-  static constexpr int CTAS = (G == 2 || Gm::NT >= 256) ? (G == 2 ? 2 : 1) : 256 / Gm::NT;
+  // registers at most per 128 threads, G = 2 launches capped at two CTAs per SM, the three-CTA
+  // layout at three)
+  static constexpr int CTAS = TRIO ? 3 : (G == 2 || Gm::NT >= 256) ? (G == 2 ? 2 : 1) : 256 / Gm::NT;
+  static constexpr int MINB = TRIO ? 3 : (G == 2 ? 2 : 1);   // the kernel's register cap
   static constexpr int BUDGET = 228 * 1024 / CTAS - 1024 < 227 * 1024 ? 228 * 1024 / CTAS - 1024 : 227 * 1024;
   // GA = 1: chunk i + 1's gate pass runs inside chunk i's reverse pass, so the gate products are
   // double-buffered; layouts that would lose a CTA per SM that way keep one gate buffer (GA = 0)
@@ -107,7 +116,8 @@ struct BwdSmem {
   static constexpr int BYTES = OFF_BAR + NSTAGE * 8;
   static_assert(ACT % 128 == 0 && BC % 128 == 0, "TMA tiles must stay 128-byte aligned");
   static_assert(OFF_CF % 16 == 0, "coefficient slots must stay 16-byte aligned");
-  static_assert(N != 16 || G != 4 || CACHE, "the N = 16 layout keeps its coefficients");
+  static_assert(N != 16 || G != 4 || CACHE || TRIO, "the fp32 N = 16 layout keeps its coefficients");
+  static_assert(!TRIO || BYTES <= BUDGET, "the three-CTA layout must fit three CTAs per SM");
   static_assert(BYTES <= 227 * 1024, "backward shared-memory layout exceeds a CTA's limit");
 };
 
@@ -171,9 +181,10 @@ __device__ __forceinline__ float2 zoh_rho(float2 x, float2 a, float2 iA) {
   return mul2(make_float2(fmaxf(rp.x, rm.x), fmaxf(rp.y, rm.y)), iA);
 }
 
-// G = 2 exists to raise occupancy, so its register budget is capped at two CTAs per SM.
+// G = 2 exists to raise occupancy, so its register budget is capped at two CTAs per SM; the bf16
+// N = 16 layout is capped at three.
 template <int N, int G, int METHOD, typename T>
-__global__ void __launch_bounds__(Geo<N, G>::NT, (G == 2 ? 2 : 1)) ssm_bwd_kernel(const __grid_constant__ BwdParams p) {
+__global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd_kernel(const __grid_constant__ BwdParams p) {
   using Gm = Geo<N, G>;
   using S = BwdSmem<N, G, T>;
   constexpr int TC = Gm::TC, DT = Gm::DT, LPC = Gm::LPC, CPW = Gm::CPW, NW = Gm::NW, NT = Gm::NT;

@@ -49,10 +49,12 @@ struct FwdSmem {
   static constexpr int OFF_U = 0, OFF_DT = ACT, OFF_Z = 2 * ACT, OFF_B = 3 * ACT, OFF_C = 3 * ACT + BC;
   static constexpr int STAGE = 3 * ACT + 2 * BC;
   static constexpr int OFF_BAR = NSTAGE * STAGE;
-  static constexpr int OFF_SDT = OFF_BAR + NSTAGE * 8;   // dt_softplus: the box's activated deltas (fp32)
+  // the tile's step sizes as fp32 (activated when dt_softplus; bf16 always), and for bf16 its u
+  static constexpr int OFF_SDT = OFF_BAR + NSTAGE * 8;
+  static constexpr int OFF_SU = OFF_SDT + TC * BXC * 4;
   // bf16: the current box's B and C converted to fp32 once (a lane would otherwise unpack eight bf16
   // values per step); fp32 reads the staged box directly
-  static constexpr int OFF_BCF = (OFF_SDT + TC * BXC * 4 + 15) / 16 * 16;
+  static constexpr int OFF_BCF = (OFF_SU + (E == 2 ? TC * BXC * 4 : 0) + 15) / 16 * 16;
   static constexpr int BCF = (E == 2) ? 2 * TB * N * 4 : 0;
   static constexpr int BYTES = OFF_BCF + BCF;
   static_assert(ACT % 128 == 0 && BC % 128 == 0, "TMA boxes must stay 128-byte aligned");
@@ -222,8 +224,16 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
       // the gate as a select and predicated stores: no branch inside the step loop this runs in
       const float yo = p.has_z ? yv * (zz[i] * sigmoid(zz[i])) : yv;
       const bool ok = tb >= 0 && dvalid && t < p.L;
-      st_pred(ygout + (long long)t * p.yg.sl, from_f32<T>(yv), ok && p.save_ygate);
-      st_pred(yout + (long long)t * p.y.sl, from_f32<T>(yo), ok);
+      // 4-tile boxes (grids that fit the GPU at once, few warps per SM): predicated stores keep the
+      // step loop one basic block for the scheduler (config 1 forward 59.0 -> 54.1 us); 2-tile boxes
+      // (many warps per SM) keep branches (config 2: 1.09 vs 1.15 ms, config 3: 3.40 vs 3.48 ms)
+      if constexpr (KB >= 4) {
+        st_pred(ygout + (long long)t * p.yg.sl, from_f32<T>(yv), ok && p.save_ygate);
+        st_pred(yout + (long long)t * p.y.sl, from_f32<T>(yo), ok);
+      } else {
+        if (ok && p.save_ygate) ygout[(long long)t * p.yg.sl] = from_f32<T>(yv);
+        if (ok) yout[(long long)t * p.y.sl] = from_f32<T>(yo);
+      }
     }
   };
   // the previous tile's outputs wait here and are emitted from inside the next tile's step loop,
@@ -289,16 +299,21 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
     if (MODE == kModeMain && p.chunk_states != nullptr && dvalid)   // state entering chunk t0 / 16
       storep<G>(p.chunk_states + (((size_t)b * p.nchunks + t0 / TC) * p.D + d) * N + nbase, h);
 
-    // dt_softplus: the box's deltas are activated once per element, softplus(raw + bias), into an
-    // fp32 tile (rows past L and columns past D stay 0: identity steps).  The previous box's
-    // readers are done: every lane passed the __syncwarp before that box's refill.
+    // The tile's deltas go once per element into an fp32 tile: activated, softplus(raw + bias), when
+    // dt_softplus (rows past L and columns past D stay 0: identity steps), else (bf16) converted; bf16
+    // also converts u.  The step loop then reads fp32 without per-step conversions (each value is
+    // read by the LPC lanes of its channel).  The previous tile's readers are done: every lane
+    // passed the __syncwarp at the end of that tile.
     float* const SDT = reinterpret_cast<float*>(smem + S::OFF_SDT);
-    if (p.dt_softplus) {
+    float* const SU = reinterpret_cast<float*>(smem + S::OFF_SU);
+    if (p.dt_softplus || sizeof(T) == 2) {
       for (int e = lane; e < TC * BXC; e += 32) {
         const int t = t0 + e / BXC, dg = x0 + e % BXC;
-        SDT[e] = (t < p.L && dg < p.D)
-                     ? softplus(to_f32(DLs[e]) + (p.dt_bias != nullptr ? p.dt_bias[dg] : 0.0f))
-                     : 0.0f;
+        const float raw = to_f32(DLs[e]);
+        SDT[e] = !p.dt_softplus ? raw
+                 : (t < p.L && dg < p.D) ? softplus(raw + (p.dt_bias != nullptr ? p.dt_bias[dg] : 0.0f))
+                                         : 0.0f;
+        if constexpr (sizeof(T) == 2) SU[e] = to_f32(Xs[e]);
       }
       __syncwarp();
     }
@@ -309,7 +324,14 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
       if constexpr (sizeof(T) == 4) {
         return dsrc[i];
       } else {
-        return p.dt_softplus ? SDT[i] : to_f32(DLs[i]);
+        return SDT[i];
+      }
+    };
+    auto u_at = [&](int i) -> float {   // u (the adjoint pass: dy)
+      if constexpr (sizeof(T) == 4) {
+        return Xs[i];
+      } else {
+        return SU[i];
       }
     };
 
@@ -322,7 +344,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
 #pragma unroll
         for (int q = 0; q < kFwdSub; ++q) {
           const int tt = t0s + q;
-          float dys = to_f32(Xs[tt * BXC + dl]);
+          float dys = u_at(tt * BXC + dl);
           const float dtv = delta_at(tt * BXC + dl);
           if (p.has_z) {
             const float zz = to_f32(Zs[tt * BXC + dl]);
@@ -361,7 +383,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
 #pragma unroll
         for (int q = 0; q < kFwdSub; ++q) {
           const int tt = base + q;
-          fu[slot][q] = to_f32(Xs[tt * BXC + dl]);
+          fu[slot][q] = u_at(tt * BXC + dl);
           fdt[slot][q] = delta_at(tt * BXC + dl);
           loadp<G>(Bs + tt * N + nbase, fB[slot][q]);
           if (MODE == kModeMain) loadp<G>(Cs + tt * N + nbase, fC[slot][q]);
@@ -406,7 +428,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
 #pragma unroll
         for (int i = 0; i < YPL; ++i) {
           zk[i] = to_f32(Zs[(g + i * LPC) * BXC + dl]);
-          uk[i] = to_f32(Xs[(g + i * LPC) * BXC + dl]);
+          uk[i] = u_at((g + i * LPC) * BXC + dl);
         }
       }
     }
