@@ -118,8 +118,17 @@ SSM_API int ssm_scan_fwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t met
  * reproducible run to run (the reference needs torch.use_deterministic_algorithms
  * for that, kernels/triton_scan.py:298-302).
  * workspace: at least ssm_scan_bwd_workspace_size() bytes.
+ * A long sequence over few (batch, 32-channel) tiles is split into segments that run at the
+ * same time (ssm_scan_bwd_plan); the workspace size covers the split.
  * ------------------------------------------------------------------------------- */
 SSM_API int ssm_scan_bwd_workspace_size(int64_t B, int64_t L, int64_t D, int64_t N, size_t* bytes);
+
+/* The backward's sequence split for a shape on the current device: *nseg segments of *seg_len
+ * steps (a multiple of 16; *nseg = 1: no split).  The reference's backward runs one program per
+ * (batch, channel block) over the whole sequence (kernels/triton_scan.py:288-319); this query has
+ * no reference counterpart.  dtype: SSM_F32 or SSM_BF16. */
+SSM_API int ssm_scan_bwd_plan(int64_t B, int64_t L, int64_t D, int64_t N, int32_t dtype, int32_t* nseg,
+                              int32_t* seg_len);
 
 SSM_API int ssm_scan_bwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method,
                  ssm_view u, ssm_view delta, const float* A, ssm_view Bm, ssm_view Cm,

@@ -26,6 +26,7 @@ EXPORTED = (
     "ssm_scan_fwd_summary", "ssm_scan_fwd_finish", "ssm_state_update", "ssm_scan_bwd_noalloc",
     "ssm_scan_bwd_summary", "ssm_conv1d_fwd", "ssm_conv1d_bwd_workspace_size", "ssm_conv1d_bwd",
     "selective_scan_fwd", "selective_scan_bwd", "selective_state_update", "ssm_scan_fwd_ex", "ssm_scan_bwd_ex",
+    "ssm_scan_bwd_plan",
 )
 
 
@@ -57,6 +58,7 @@ _SIGNATURES = {
     "ssm_read_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32)]),
     "ssm_scan_fwd_workspace_size": (ctypes.c_int, [_I64, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
     "ssm_scan_bwd_workspace_size": (ctypes.c_int, [_I64, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
+    "ssm_scan_bwd_plan": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, ctypes.POINTER(_I32), ctypes.POINTER(_I32)]),
     "ssm_scan_fwd": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _V, _P, _V, _V, _P, _V, _P,
                                     _V, _V, _P, _P, _P, _SZ, _P]),
     "ssm_scan_fwd_summary": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _V, _P, _V, _P, _P,
@@ -168,6 +170,14 @@ def fwd_workspace_bytes(B, L, D, N):
     n = _SZ(0)
     check(lib().ssm_scan_fwd_workspace_size(B, L, D, N, ctypes.byref(n)), "ssm_scan_fwd_workspace_size")
     return n.value
+
+
+def bwd_plan(B, L, D, N, dtype):
+    """(segments, steps per segment) of the backward's sequence split on the current device."""
+    S, n = _I32(0), _I32(0)
+    code = SSM_BF16 if dtype == torch.bfloat16 else SSM_F32
+    check(lib().ssm_scan_bwd_plan(B, L, D, N, code, ctypes.byref(S), ctypes.byref(n)), "ssm_scan_bwd_plan")
+    return S.value, n.value
 
 
 def bwd_workspace_bytes(B, L, D, N):

@@ -171,19 +171,71 @@ void plan_segments(int64_t B, int64_t L, int64_t D, int64_t N, int* nseg, int* s
   *seg_len = (int)len;
 }
 
+// Sequence split of the backward.  One CTA per (batch, 32 channels) walks the whole sequence; when
+// those CTAs fill at most 3/4 of the slots the GPU has for them (B = 1, D = 512: 16 CTAs; config 3
+// sharded over 8 GPUs: 160, over 4: 320 of 444), the sequence is cut into S segments, one CTA each: enough to fill the
+// slots once, and segments of at most 16 chunks (256 steps; more, shorter segments balance better),
+// but at least 8 chunks each.  Measured on one B200 (backward ms, S): B=1 L=4096 D=512 fp32 0.819 (1),
+// 0.166 (8), 0.109 (18), 0.114 (32); B=4 L=4096 D=512 fp32 0.794 (1), 0.371 (4), 0.332 (16);
+// B=8 L=8192 D=640 bf16 2.25 (1), 1.62 (5), 1.50 (8), 1.48 (16), 1.47 (24); B=8 L=8192 D=1280 bf16
+// 3.21 (1), 2.82 (16); config 1 (256 CTAs of 296 slots) 0.146 (1), 0.174 (2): not split.  The split costs the
+// adjoint summaries of segments 1 .. S-1 (the forward kernel's adjoint mode) and a reverse carry.
+int64_t bwd_ctas_per_sm(int64_t N, int dtype) {
+  switch (N) {
+    case 4: return 8;
+    case 8: return 4;
+    case 16: return dtype == SSM_BF16 ? 3 : 2;
+    default: return 1;
+  }
+}
+void plan_bwd_segments(int64_t B, int64_t L, int64_t D, int64_t N, int dtype, int* nseg, int* seg_len) {
+  const int64_t ctas = B * ((D + 31) / 32);
+  const int64_t slots = bwd_ctas_per_sm(N, dtype) * sm_count();
+  const int64_t nchunk = (L + kChunk - 1) / kChunk;
+  int64_t S = 1;
+  if (4 * ctas <= 3 * slots && nchunk >= 16) S = std::min<int64_t>(std::max<int64_t>(slots / ctas, nchunk / 16), nchunk / 8);
+  if (const char* env = getenv("SSM_B200_BWD_SEGMENTS")) {   // override, for measurements
+    const long v = strtol(env, nullptr, 10);
+    if (v >= 1) S = std::min<int64_t>(v, nchunk);
+  }
+  if (S < 1) S = 1;
+  int64_t len = ((L + S - 1) / S + kChunk - 1) / kChunk * kChunk;
+  S = (L + len - 1) / len;
+  *nseg = (int)S;
+  *seg_len = (int)len;
+}
+
+// Workspace arrays are carved at 256-byte boundaries (carve below): a size counts the alignment of the
+// base pointer and every array rounded up.
+size_t carved(size_t nfloat) { return (nfloat * sizeof(float) + 255) / 256 * 256; }
+size_t seg_ws_bytes(int64_t B, int64_t S, int64_t D, int64_t N) { return 256 + 3 * carved((size_t)B * S * D * N); }
+
 size_t fwd_ws_bytes(int64_t B, int64_t L, int64_t D, int64_t N) {
   int S, len;
   plan_segments(B, L, D, N, &S, &len);
   if (S <= 1) return 0;
-  return 3 * (size_t)B * S * D * N * sizeof(float) + 256;
+  return seg_ws_bytes(B, S, D, N);
 }
 
-size_t bwd_ws_bytes(int64_t B, int64_t L, int64_t D, int64_t N) {
+// Workspace of a backward with S segments: the dB | dC partials, the (batch, segment) partials of
+// dA, dD and d(bias), and for S > 1 the incoming adjoints and the adjoint pass's three segment
+// arrays (decay, adjoint from zero, carry).
+size_t bwd_ws_bytes_for(int64_t B, int64_t L, int64_t D, int64_t N, int64_t S) {
   const int64_t ndt = (D + 31) / 32;
-  const size_t bc = (size_t)B * ndt * L * 2 * N;
-  const size_t a = (size_t)B * D * N;
-  const size_t dd = (size_t)B * D;
-  return (bc + a + 2 * dd) * sizeof(float) + 4 * 256;   // + (B, D) dt_bias partials
+  const size_t own = 256 + carved((size_t)B * ndt * L * 2 * N) + carved((size_t)B * S * D * N) +
+                     2 * carved((size_t)B * S * D);
+  const size_t segs = S > 1 ? carved((size_t)B * S * D * N) + seg_ws_bytes(B, S, D, N) : 0;
+  return own + segs;
+}
+// the size the API reports: enough for either element type's segment plan
+size_t bwd_ws_bytes(int64_t B, int64_t L, int64_t D, int64_t N) {
+  size_t need = 0;
+  for (int dtype : {SSM_F32, SSM_BF16}) {
+    int S, len;
+    plan_bwd_segments(B, L, D, N, dtype, &S, &len);
+    need = std::max(need, bwd_ws_bytes_for(B, L, D, N, S));
+  }
+  return need;
 }
 
 float* carve(unsigned char*& cur, size_t nfloat) {
@@ -223,11 +275,14 @@ int check_f32(const char* name, const void* p, bool required) {
 // Shared body of ssm_scan_fwd / ssm_scan_fwd_finish / ssm_scan_fwd_summary.
 // phase: 0 = full forward, 1 = summary only (writes decay/hend), 2 = finish (reuses the
 // per-segment summaries a phase-1 call left in the workspace), 3 = adjoint summary (u carries
-// dy and Bm carries C; writes decay and the adjoint at the sequence start into decay/hend).
+// dy and Bm carries C; writes decay and the adjoint at the sequence start into decay/hend),
+// 4 = the backward's segment adjoints: the adjoint summaries of the given plan_S segments of plan_len
+// steps composed in reverse from h0 (dlast), the adjoint entering every segment written to seg_out.
 int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, ssm_view u, ssm_view delta,
              const float* A, ssm_view Bm, ssm_view Cm, const float* Dskip, ssm_view z, const float* h0,
              ssm_view y, ssm_view ygate, float* last, float* chunk_states, float* tot_decay, float* tot_hend,
-             void* workspace, size_t workspace_bytes, void* stream_v, const ssm_delta_opts* opts = nullptr) {
+             void* workspace, size_t workspace_bytes, void* stream_v, const ssm_delta_opts* opts = nullptr,
+             int plan_S = 0, int plan_len = 0, float* seg_out = nullptr) {
   int rc = check_common(B, L, D, N, method);
   if (rc) return rc;
   if (u.ptr == nullptr) return fail(SSM_ERR_INVALID, "u is required");
@@ -235,8 +290,9 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   if (dt != SSM_F32 && dt != SSM_BF16) return fail(SSM_ERR_DTYPE, "u dtype %d unsupported", dt);
   if ((rc = check_view("delta", delta, dt, D, true))) return rc;
   if ((rc = check_view("Bm", Bm, dt, N, true))) return rc;
-  const bool summary = (phase == 1 || phase == 3);
-  if (phase == 3 && (rc = check_view("z", z, dt, D, false))) return rc;
+  const bool summary = (phase == 1 || phase == 3 || phase == 4);
+  const bool adjoint = (phase == 3 || phase == 4);
+  if (adjoint && (rc = check_view("z", z, dt, D, false))) return rc;
   if (!summary) {
     if ((rc = check_view("Cm", Cm, dt, N, true))) return rc;
     if ((rc = check_view("z", z, dt, D, false))) return rc;
@@ -248,9 +304,11 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   if ((rc = check_f32("h0", h0, false))) return rc;
   if ((rc = check_f32("last", last, false))) return rc;
   if ((rc = check_f32("chunk_states", chunk_states, false))) return rc;
-  if (summary && (tot_decay == nullptr || tot_hend == nullptr || !aligned16(tot_decay) || !aligned16(tot_hend)))
+  if ((phase == 1 || phase == 3) &&
+      (tot_decay == nullptr || tot_hend == nullptr || !aligned16(tot_decay) || !aligned16(tot_hend)))
     return fail(SSM_ERR_INVALID, "the two summary outputs are required and must be 16-byte aligned");
-  const size_t need = fwd_ws_bytes(B, L, D, N);
+  if (phase == 4 && (plan_S < 2 || seg_out == nullptr)) return fail(SSM_ERR_INVALID, "segment adjoints need S > 1");
+  const size_t need = phase == 4 ? seg_ws_bytes(B, plan_S, D, N) : fwd_ws_bytes(B, L, D, N);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need))
     return fail(SSM_ERR_WORKSPACE, "forward workspace of %zu bytes required, %zu given", need, workspace_bytes);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
@@ -289,7 +347,12 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   if (!summary) use_tma = use_tma && tma_ok(Cm, B, L, N);
   if (phase != 1) use_tma = use_tma && (!p.has_z || tma_ok(z, B, L, D));
   int S, len;
-  plan_segments(B, L, D, N, &S, &len);
+  if (phase == 4) {
+    S = plan_S;
+    len = plan_len;
+  } else {
+    plan_segments(B, L, D, N, &S, &len);
+  }
   p.nseg = S;
   p.seg_len = len;
   // TMA boxes of kb 16-step tiles: 4 for an unsplit main pass whose warps (one per CTA) all fit on
@@ -312,12 +375,14 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
   const unsigned ndt = (unsigned)((D + 31) / 32);
   const dim3 grid(ndt, (unsigned)S, (unsigned)B);
   auto launch = [&](int mode, const FwdParams& q) {
-    return bf ? launch_fwd<__nv_bfloat16>((int)N, G, method, mode, kb, q, grid, stream)
-              : launch_fwd<float>((int)N, G, method, mode, kb, q, grid, stream);
+    // segments [seg_first, S): the backward's segment adjoints skip segment 0 (nothing precedes it)
+    const dim3 g(grid.x, grid.y - (unsigned)q.seg_first, grid.z);
+    return bf ? launch_fwd<__nv_bfloat16>((int)N, G, method, mode, kb, q, g, stream)
+              : launch_fwd<float>((int)N, G, method, mode, kb, q, g, stream);
   };
   cudaError_t e;
 
-  const int smode = (phase == 3) ? kModeAdjoint : kModeSummary;
+  const int smode = adjoint ? kModeAdjoint : kModeSummary;
   if (S == 1) {
     if (summary) {
       FwdParams q = p;
@@ -341,21 +406,22 @@ int fwd_impl(int phase, int64_t B, int64_t L, int64_t D, int64_t N, int32_t meth
     FwdParams q = p;
     q.seg_hend = seg_hend;
     q.seg_decay = seg_decay;
+    q.seg_first = phase == 4 ? 1 : 0;   // the reverse carry never uses segment 0's summary
     if ((e = launch(smode, q)) != cudaSuccess) return cuda_fail(e, "summary launch");
   }
   CarryParams cp;
   memset(&cp, 0, sizeof(cp));
-  cp.h_init = summary ? nullptr : h0;
+  cp.h_init = (summary && phase != 4) ? nullptr : h0;
   cp.seg_decay = seg_decay;
   cp.seg_hend = seg_hend;
-  cp.seg_init = summary ? nullptr : seg_init;
-  cp.tot_decay = summary ? tot_decay : nullptr;
-  cp.tot_hend = summary ? tot_hend : nullptr;
+  cp.seg_init = phase == 4 ? seg_out : summary ? nullptr : seg_init;
+  cp.tot_decay = (summary && phase != 4) ? tot_decay : nullptr;
+  cp.tot_hend = (summary && phase != 4) ? tot_hend : nullptr;
   cp.B = (int)B;
   cp.D = (int)D;
   cp.N = (int)N;
   cp.nseg = S;
-  cp.reverse = (phase == 3) ? 1 : 0;
+  cp.reverse = adjoint ? 1 : 0;
   if ((e = launch_carry(cp, stream)) != cudaSuccess) return cuda_fail(e, "carry launch");
   if (summary) return SSM_OK;
   p.seg_init = seg_init;
@@ -399,6 +465,18 @@ int ssm_scan_bwd_workspace_size(int64_t B, int64_t L, int64_t D, int64_t N, size
   int rc = check_common(B, L, D, N, SSM_ZOH);
   if (rc) return rc;
   *bytes = bwd_ws_bytes(B, L, D, N);
+  return SSM_OK;
+}
+
+int ssm_scan_bwd_plan(int64_t B, int64_t L, int64_t D, int64_t N, int32_t dtype, int32_t* nseg, int32_t* seg_len) {
+  if (nseg == nullptr || seg_len == nullptr) return fail(SSM_ERR_INVALID, "nseg and seg_len are required");
+  int rc = check_common(B, L, D, N, SSM_ZOH);
+  if (rc) return rc;
+  if (dtype != SSM_F32 && dtype != SSM_BF16) return fail(SSM_ERR_DTYPE, "dtype %d unsupported", (int)dtype);
+  int S, len;
+  plan_bwd_segments(B, L, D, N, dtype, &S, &len);
+  *nseg = S;
+  *seg_len = len;
   return SSM_OK;
 }
 
@@ -510,7 +588,9 @@ int ssm_scan_bwd_ex(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, 
   if ((rc = check_f32("dA", dA, true))) return rc;
   if ((rc = check_f32("dDskip", dDskip, Dskip != nullptr))) return rc;
   if ((rc = check_f32("dh0", dh0, h0 != nullptr))) return rc;
-  const size_t need = bwd_ws_bytes(B, L, D, N);
+  int S, seg_len;
+  plan_bwd_segments(B, L, D, N, dt, &S, &seg_len);
+  const size_t need = bwd_ws_bytes_for(B, L, D, N, S);
   if (workspace == nullptr || workspace_bytes < need)
     return fail(SSM_ERR_WORKSPACE, "backward workspace of %zu bytes required, %zu given", need, workspace_bytes);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
@@ -543,13 +623,26 @@ int ssm_scan_bwd_ex(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, 
   p.has_z = has_z ? 1 : 0;
   unsigned char* cur = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
   p.part_bc = carve(cur, (size_t)B * ndt * L * 2 * N);
-  p.part_A = carve(cur, (size_t)B * D * N);
-  p.part_D = carve(cur, (size_t)B * D);
-  p.part_dtb = carve(cur, (size_t)B * D);
+  p.part_A = carve(cur, (size_t)B * S * D * N);
+  p.part_D = carve(cur, (size_t)B * S * D);
+  p.part_dtb = carve(cur, (size_t)B * S * D);
+  p.nseg = S;
+  p.seg_len = seg_len;
   if (opts != nullptr && opts->softplus) {
     if (opts->bias != nullptr && !aligned16(opts->bias)) return fail(SSM_ERR_INVALID, "delta bias must be 16-byte aligned");
     p.dt_softplus = 1;
     p.dt_bias = opts->bias;
+  }
+  if (S > 1) {   // the adjoint entering every segment: summaries of the later segments, composed in reverse
+    float* seg_dh = carve(cur, (size_t)B * S * D * N);
+    const size_t used = (size_t)(cur - static_cast<unsigned char*>(workspace));
+    ssm_view none;
+    memset(&none, 0, sizeof(none));
+    none.dtype = dt;
+    rc = fwd_impl(4, B, L, D, N, method, dy, delta, A, Cm, none, nullptr, z, dlast, none, none, nullptr, nullptr,
+                  nullptr, nullptr, cur, workspace_bytes - used, stream_v, opts, S, seg_len, seg_dh);
+    if (rc) return rc;
+    p.seg_dh = seg_dh;
   }
 
   bool use_tma = tma_ok(u, B, L, D) && tma_ok(delta, B, L, D) && tma_ok(dy, B, L, D) && tma_ok(Bm, B, L, N) &&
@@ -564,7 +657,7 @@ int ssm_scan_bwd_ex(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, 
   p.use_tma = use_tma ? 1 : 0;
 
   const bool bf = dt == SSM_BF16;
-  const dim3 grid((unsigned)ndt, (unsigned)B, 1);
+  const dim3 grid((unsigned)ndt, (unsigned)B, (unsigned)S);
   const int G = choose_g(B, D, N);
   cudaError_t e = bf ? launch_bwd<__nv_bfloat16>((int)N, G, method, p, grid, stream)
                      : launch_bwd<float>((int)N, G, method, p, grid, stream);
@@ -586,6 +679,7 @@ int ssm_scan_bwd_ex(int64_t B, int64_t L, int64_t D, int64_t N, int32_t method, 
   f.D = (int)D;
   f.N = (int)N;
   f.ndt = ndt;
+  f.nsum = (int)(B * S);
   e = bf ? launch_bwd_finalize<__nv_bfloat16>(f, stream) : launch_bwd_finalize<float>(f, stream);
   if (e != cudaSuccess) return cuda_fail(e, "backward finalize launch");
   return SSM_OK;

@@ -5,7 +5,11 @@
 // models/scan.py:219-255 (reverse adjoint scan dh_t = g_t + a_{t+1} dh_{t+1}, then gradients
 // through discretize).
 //
-// One CTA owns a (batch, 32-channel tile) and walks the sequence backwards in 16-step chunks.
+// One CTA owns a (batch, 32-channel tile, sequence segment) and walks its segment backwards in
+// 16-step chunks.  Grids with fewer CTAs than the GPU holds at once (long sequences over few
+// channels) split the sequence into segments: each starts from the adjoint entering it from the
+// right, which the adjoint summaries of the later segments give (the forward kernel's adjoint mode
+// and the reverse carry; one segment takes dlast).
 // For every chunk it
 //   (1) TMA-stages u, delta, z, dy, the saved pre-gate output and B, C;
 //   (2) gate pass, once per (t, d): dys = dy silu(z), dz (stored straight to global memory), dD,
@@ -215,7 +219,11 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
   const int b = blockIdx.y, dtile = blockIdx.x;
   const int d0 = dtile * DT, d = d0 + dl;
   const bool dvalid = d < p.D;
-  const int nch = p.nchunks;
+  // the CTA's sequence segment (blockIdx.z): chunks [ctop - nch + 1, ctop], walked from ctop down
+  const int seg = blockIdx.z;
+  const int c_first = seg * (p.seg_len / TC);
+  const int ctop = min(p.nchunks, c_first + p.seg_len / TC) - 1;
+  const int nch = ctop + 1 - c_first;
   const int nbase = g * G;
   // register slot j holds state nbase + (j ^ perm); slot bit (LG-1-s) = c bit (LC-1-s)
   int perm = 0;
@@ -241,10 +249,15 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
   }
   const float Dd = (p.Dskip != nullptr && dvalid) ? p.Dskip[d] : 0.0f;
   const size_t bd = ((size_t)b * p.D + d) * N + nbase;
+  const size_t bsd = (size_t)b * p.nseg + seg;            // (batch, segment) partial group
+  const size_t pbd = (bsd * p.D + d) * N + nbase;
 
   float2 dh[NP], dAA[NP];
-  if (p.dlast != nullptr) {
-    slot_load(p.dlast + bd, dh);
+  // the adjoint entering the segment from its right: dlast for the last segment, else the composed
+  // adjoint summaries of the segments after it
+  const float* const dh_in = (seg == p.nseg - 1) ? (p.dlast != nullptr ? p.dlast + bd : nullptr) : p.seg_dh + pbd;
+  if (dh_in != nullptr) {
+    slot_load(dh_in, dh);
   } else {
 #pragma unroll
     for (int i = 0; i < NP; ++i) dh[i] = bc2(0.f);
@@ -265,7 +278,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
     __syncthreads();
     if (tid == 0) {
       for (int s = 0; s < S::NSTAGE && s < nch; ++s)
-        bwd_issue_loads<S>(p, smem + s * S::STAGE, &bars[s], d0, (nch - 1 - s) * TC, b);
+        bwd_issue_loads<S>(p, smem + s * S::STAGE, &bars[s], d0, (ctop - s) * TC, b);
     }
   }
 
@@ -275,7 +288,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
     if (p.use_tma) {
       mbar_wait(&bars[ci % S::NSTAGE], (uint32_t)((ci / S::NSTAGE) & 1), p.err);
     } else {
-      bwd_coop_load<S, N, NT, T>(p, smem + (ci % S::NSTAGE) * S::STAGE, d0, (nch - 1 - ci) * TC, b);
+      bwd_coop_load<S, N, NT, T>(p, smem + (ci % S::NSTAGE) * S::STAGE, d0, (ctop - ci) * TC, b);
       __syncthreads();
     }
   };
@@ -293,7 +306,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
     const T* DYs = reinterpret_cast<const T*>(stg + S::OFF_DY);
     const T* YGs = reinterpret_cast<const T*>(stg + S::OFF_YG);
     const int e = tid + k * NT;
-    const int t = (nch - 1 - ci) * TC + e / DT, dg = d0 + e % DT;
+    const int t = (ctop - ci) * TC + e / DT, dg = d0 + e % DT;
     const float dyv = to_f32(DYs[e]);
     const float uu = to_f32(Xs[e]);
     // z terms as selects: without z the Z and YG tiles hold stale values that are never
@@ -345,7 +358,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
     __syncthreads();
     if (p.use_tma && tid == 0) {
       for (int c0 = S::NSTAGE; c0 < S::NSTAGE + GA && c0 < nch; ++c0)
-        bwd_issue_loads<S>(p, smem + (c0 % S::NSTAGE) * S::STAGE, &bars[c0 % S::NSTAGE], d0, (nch - 1 - c0) * TC, b);
+        bwd_issue_loads<S>(p, smem + (c0 % S::NSTAGE) * S::STAGE, &bars[c0 % S::NSTAGE], d0, (ctop - c0) * TC, b);
     }
   }
 
@@ -408,7 +421,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
     }
   };
 
-  auto cs_ptr = [&](int ch) { return p.chunk_states + (((size_t)b * nch + ch) * p.D + d) * N + nbase; };
+  auto cs_ptr = [&](int ch) { return p.chunk_states + (((size_t)b * p.nchunks + ch) * p.D + d) * N + nbase; };
   auto cs_load = [&](int ch, float2 (&o)[NP]) {   // the state entering chunk ch (zero before chunk 0)
     if (ch >= 0) {
       slot_load(cs_ptr(ch), o);
@@ -418,11 +431,11 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
     }
   };
   float2 hs[NP];                          // the state entering chunk i
-  cs_load(nch - 1, hs);
+  cs_load(ctop, hs);
 
   {
     for (int i = 0; i < nch; ++i) {
-      const int ch = nch - 1 - i;
+      const int ch = ctop - i;
       const int t0 = ch * TC;
       float2 hs_next[NP];                 // the state entering chunk i + 1
       cs_load(ch - 1, hs_next);
@@ -639,7 +652,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
       if (p.use_tma && tid == 0) {        // the stage just consumed takes chunk nx
         const int nx = i + GA + S::NSTAGE;
         if (nx < nch)
-          bwd_issue_loads<S>(p, smem + (nx % S::NSTAGE) * S::STAGE, &bars[nx % S::NSTAGE], d0, (nch - 1 - nx) * TC, b);
+          bwd_issue_loads<S>(p, smem + (nx % S::NSTAGE) * S::STAGE, &bars[nx % S::NSTAGE], d0, (ctop - nx) * TC, b);
       }
       store_tile<NT, S::OP>(DUo, p.du, b, t0, d0, p.L, p.D);
       store_tile<NT, S::OP>(DDTo, p.ddt, b, t0, d0, p.L, p.D);
@@ -648,16 +661,16 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
     }
   }
 
-  // per-(b, d) partials; ssm_bwd_finalize sums them over b in fixed order
+  // per-(b, segment, d) partials; ssm_bwd_finalize sums them over (b, segment) in fixed order
   SDD[tid] = dDacc;
   __syncthreads();
   if (dvalid) {
 #pragma unroll
     for (int k = 0; k < NP; ++k) {
       const float2 da = (METHOD == kZOH) ? mul2(dAA[k], iA[k]) : dAA[k];
-      p.part_A[bd + ((2 * k) ^ perm)] = da.x;
-      p.part_A[bd + ((2 * k + 1) ^ perm)] = da.y;
-      if (p.dh0 != nullptr) {
+      p.part_A[pbd + ((2 * k) ^ perm)] = da.x;
+      p.part_A[pbd + ((2 * k + 1) ^ perm)] = da.y;
+      if (p.dh0 != nullptr && seg == 0) {
         p.dh0[bd + ((2 * k) ^ perm)] = dh[k].x;
         p.dh0[bd + ((2 * k + 1) ^ perm)] = dh[k].y;
       }
@@ -666,16 +679,16 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
   if (tid < DT && d0 + tid < p.D) {
     float sdd = 0.f;
     for (int w = 0; w < NT / DT; ++w) sdd += SDD[w * DT + tid];
-    p.part_D[(size_t)b * p.D + d0 + tid] = sdd;
+    p.part_D[bsd * p.D + d0 + tid] = sdd;
   }
   if (p.dt_softplus && p.part_dtb != nullptr) {   // the channel's share sits on its LPC lanes
     const float t = group_allreduce<LPC, 1>(dtbacc);
-    if (g == 0 && dvalid) p.part_dtb[(size_t)b * p.D + d] = t;
+    if (g == 0 && dvalid) p.part_dtb[bsd * p.D + d] = t;
   }
 }
 
 // Sums the per-CTA dB | dC partials over channel tiles and the dA / dD / step-size-bias partials
-// over batch, each in a fixed order (loads of a group of kU terms are issued together, then added in
+// over (batch, segment), each in a fixed order (loads of a group of kU terms are issued together, then added in
 // index order), and writes dB, dC (element type T), dA, dD, d(bias) (fp32).  dB | dC: one warp per
 // (b, t) row, lanes over its 2N values (coalesced, one index division per row); the rest: one
 // thread per output.
@@ -718,11 +731,11 @@ __global__ void ssm_bwd_finalize(const FinParams p) {
   const long long total = nA + nDD + (p.ddt_bias != nullptr ? p.D : 0);
   for (long long i = gtid; i < total; i += nthr) {
     if (i < nA) {
-      p.dA[i] = sum(p.part_A + i, (size_t)nA, p.B);
+      p.dA[i] = sum(p.part_A + i, (size_t)nA, p.nsum);
     } else if (i < nA + nDD) {
-      p.dD[i - nA] = sum(p.part_D + (i - nA), (size_t)p.D, p.B);
+      p.dD[i - nA] = sum(p.part_D + (i - nA), (size_t)p.D, p.nsum);
     } else {
-      p.ddt_bias[i - nA - nDD] = sum(p.part_dtb + (i - nA - nDD), (size_t)p.D, p.B);
+      p.ddt_bias[i - nA - nDD] = sum(p.part_dtb + (i - nA - nDD), (size_t)p.D, p.nsum);
     }
   }
 }

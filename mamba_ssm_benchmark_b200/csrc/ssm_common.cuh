@@ -343,6 +343,7 @@ struct alignas(64) FwdParams {
   const float* dt_bias;      // (D) or null: added to delta before the softplus
   int* err;
   int B, L, D, nchunks, seg_len, nseg;
+  int seg_first;             // segment of blockIdx.y = 0 (grids over a suffix of the segments)
   int has_z, use_tma, save_ygate;
   int dt_softplus;           // delta = softplus(delta + dt_bias) in the kernel
 };
@@ -355,14 +356,16 @@ struct alignas(64) BwdParams {
   const float* h0;           // (B, D, N) or null (only for dh0 presence)
   const float* chunk_states; // (B, nchunks, D, N)
   const float* dlast;        // (B, D, N) or null
+  const float* seg_dh;       // (B, S, D, N) or null: the adjoint entering each segment from its right (S > 1)
   float* dh0;                // (B, D, N) or null
   float* part_bc;            // (B, nDT, L, 2N): per-CTA dB | dC partial sums
-  float* part_A;             // (B, D, N)
-  float* part_D;             // (B, D)
+  float* part_A;             // (B, S, D, N)
+  float* part_D;             // (B, S, D)
   const float* dt_bias;      // (D) or null (see FwdParams)
-  float* part_dtb;           // (B, D): per-batch sums of the raw-delta gradient (dt_softplus)
+  float* part_dtb;           // (B, S, D): per-(batch, segment) sums of the raw-delta gradient (dt_softplus)
   int* err;
   int B, L, D, nchunks, ndt;
+  int nseg, seg_len;         // sequence segments (blockIdx.z) of seg_len steps, a multiple of 16
   int has_z, use_tma;
   int dt_softplus;           // ddt is then the gradient w.r.t. the raw delta: ddelta * sigmoid(raw + bias)
 };
@@ -374,9 +377,10 @@ struct FinParams {
   DAct dB, dC;               // outputs (B, L, N), element type T
   float* dA;                 // (D, N)
   float* dD;                 // (D) or null
-  const float* part_dtb;     // (B, D) or null
+  const float* part_dtb;     // (B, S, D) or null
   float* ddt_bias;           // (D) or null
   int B, L, D, N, ndt;
+  int nsum;                  // partial groups of dA, dD, d(bias): B x backward segments
 };
 
 struct CarryParams {

@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(32) ssm_fwd_kernel(const __grid_constant__ Fwd
   const int lane = threadIdx.x;
   const int c = lane % CPW, g = lane / CPW;
   constexpr int GSTRIDE = CPW;   // lane distance between a channel's state groups
-  const int b = blockIdx.z, seg = blockIdx.y;
+  const int b = blockIdx.z, seg = blockIdx.y + p.seg_first;
   const int d0 = blockIdx.x * CPW;
   const int x0 = (d0 / BXC) * BXC, dl = d0 - x0 + c;   // box origin and this lane's column
   const int d = d0 + c;
