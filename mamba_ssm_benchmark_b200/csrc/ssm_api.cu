@@ -164,6 +164,10 @@ void plan_segments(int64_t B, int64_t L, int64_t D, int64_t N, int* nseg, int* s
   const int64_t sms = sm_count();
   int64_t S = 1;
   if (warps < 2 * sms && nchunk >= 16) S = std::min<int64_t>((64 * sms + warps - 1) / warps, nchunk / 8);
+  if (const char* env = getenv("SSM_B200_FWD_SEGMENTS")) {   // override, for measurements
+    const long v = strtol(env, nullptr, 10);
+    if (v >= 1) S = std::min<int64_t>(v, nchunk);
+  }
   if (S < 1) S = 1;
   int64_t len = ((L + S - 1) / S + kChunk - 1) / kChunk * kChunk;
   S = (L + len - 1) / len;

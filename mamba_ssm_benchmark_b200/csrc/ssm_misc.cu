@@ -3,37 +3,68 @@
 
 namespace ssm {
 
-// Sequential composition of per-segment summaries, one thread per (b, d, n):
+// Composition of per-segment summaries, per (b, d, n):
 //   seg_init[s] = carry;  carry = decay[s] * carry + hend[s]       (s = 0 .. S-1)
 // or, for the adjoint summaries (reverse), over s = S-1 .. 0.
-// The chunk-level combine of the reference's two-level scan (models/scan.py:160-164, whose
-// log-depth Hillis-Steele pass over chunk ends is replaced by this O(S) walk per state).
-__global__ void ssm_carry_kernel(const CarryParams p) {
+// The chunk-level combine of the reference's two-level scan (models/scan.py:160-164).  A block owns
+// 32 consecutive (b, d, n) columns (coalesced) and kCarryGroups groups of consecutive segments
+// (threadIdx.y): every group composes its segments into one (decay, end) pair, the groups' pairs are
+// composed in order by one thread per column, and every group then walks its segments again from
+// its carried-in value.  Two passes over the summaries, but kCarryGroups times the loads in flight
+// of a one-thread-per-column walk, which is latency-bound (148 segments: ~30 us).
+constexpr int kCarryGroups = 16;
+__global__ void __launch_bounds__(32 * kCarryGroups) ssm_carry_kernel(const CarryParams p) {
+  __shared__ float s_dec[kCarryGroups][32], s_end[kCarryGroups][32], s_in[kCarryGroups][32];
   pdl_launch_dependents();
   pdl_wait();
   const long long dn_total = (long long)p.D * p.N;
-  const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-  if (idx >= (long long)p.B * dn_total) return;
-  const long long b = idx / dn_total, dn = idx % dn_total;
-  float carry = p.h_init != nullptr ? p.h_init[idx] : 0.0f;
-  float dec = 1.0f;
+  const long long idx = blockIdx.x * 32LL + threadIdx.x;
+  const bool live = idx < (long long)p.B * dn_total;
+  const long long b = live ? idx / dn_total : 0, dn = live ? idx % dn_total : 0;
   const size_t base = (size_t)b * p.nseg * dn_total + dn;
+  const int grp = threadIdx.y;
+  const int per = (p.nseg + kCarryGroups - 1) / kCarryGroups;
+  const int i0 = grp * per, i1 = min(p.nseg, i0 + per);          // processing positions [i0, i1)
+  auto seg_at = [&](int i) { return p.reverse ? p.nseg - 1 - i : i; };
+  float dec = 1.0f, end = 0.0f;
+  if (live) {
 #pragma unroll 4
-  for (int i = 0; i < p.nseg; ++i) {
-    const int s = p.reverse ? p.nseg - 1 - i : i;
-    const size_t o = base + (size_t)s * dn_total;
-    if (p.seg_init != nullptr) p.seg_init[o] = carry;
-    const float a = p.seg_decay[o];
-    carry = fmaf(a, carry, p.seg_hend[o]);
-    dec *= a;
+    for (int i = i0; i < i1; ++i) {
+      const size_t o = base + (size_t)seg_at(i) * dn_total;
+      const float a = p.seg_decay[o];
+      end = fmaf(a, end, p.seg_hend[o]);
+      dec *= a;
+    }
   }
-  if (p.tot_hend != nullptr) p.tot_hend[idx] = carry;
-  if (p.tot_decay != nullptr) p.tot_decay[idx] = dec;
+  s_dec[grp][threadIdx.x] = dec;
+  s_end[grp][threadIdx.x] = end;
+  __syncthreads();
+  if (grp == 0) {
+    float carry = (live && p.h_init != nullptr) ? p.h_init[idx] : 0.0f;
+    float tot = 1.0f;
+    for (int g2 = 0; g2 < kCarryGroups; ++g2) {
+      s_in[g2][threadIdx.x] = carry;
+      carry = fmaf(s_dec[g2][threadIdx.x], carry, s_end[g2][threadIdx.x]);
+      tot *= s_dec[g2][threadIdx.x];
+    }
+    if (live && p.tot_hend != nullptr) p.tot_hend[idx] = carry;
+    if (live && p.tot_decay != nullptr) p.tot_decay[idx] = tot;
+  }
+  __syncthreads();
+  if (live && p.seg_init != nullptr) {
+    float carry = s_in[grp][threadIdx.x];
+#pragma unroll 4
+    for (int i = i0; i < i1; ++i) {
+      const size_t o = base + (size_t)seg_at(i) * dn_total;
+      p.seg_init[o] = carry;
+      carry = fmaf(p.seg_decay[o], carry, p.seg_hend[o]);
+    }
+  }
 }
 
 cudaError_t launch_carry(const CarryParams& p, cudaStream_t stream) {
   const long long total = (long long)p.B * p.D * p.N;
-  return launch_pdl(ssm_carry_kernel, dim3((unsigned)((total + 127) / 128)), dim3(128), 0, stream, p);
+  return launch_pdl(ssm_carry_kernel, dim3((unsigned)((total + 31) / 32)), dim3(32, kCarryGroups), 0, stream, p);
 }
 
 // Single-token state update: the inline decode branch of Mamba.forward
