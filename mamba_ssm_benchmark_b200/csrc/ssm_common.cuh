@@ -75,7 +75,6 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
   return __float2bfloat16_rn(x);
 }
 
-// 2^x on the MUFU unit (flush-to-zero for subnormal results: the decays are in (0, 1]).
 // Global store under a predicate, as one predicated instruction (no branch, so the unrolled loop it
 // sits in stays one basic block for the scheduler).
 __device__ __forceinline__ void st_pred(float* ptr, float v, bool ok) {
@@ -86,6 +85,7 @@ __device__ __forceinline__ void st_pred(__nv_bfloat16* ptr, __nv_bfloat16 v, boo
   asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %2, 0;\n\t@p st.global.b16 [%0], %1;\n\t}" ::"l"(ptr),
                "h"(__bfloat16_as_ushort(v)), "r"((int)ok));
 }
+// 2^x on the MUFU unit (flush-to-zero for subnormal results: the decays are in (0, 1]).
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
