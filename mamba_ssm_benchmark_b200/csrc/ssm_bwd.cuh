@@ -40,7 +40,11 @@
 // two FMAs per element and stays accurate in relative terms for every z and every A, where the
 // reference evaluates f(z) = (z e^z - expm1 z) / z^2 with a series branch
 // (kernels/triton_scan.py:199-202) and forming A dA as delta dh/ddelta - coef B u would lose about
-// 1e-7 / |A| relative (1e-2 at |A| = 1e-3 in the transient of small steps).
+// 1e-7 / |A| relative (1e-2 at |A| = 1e-3 in the transient of small steps).  In the reverse pass the
+// two sums are kept apart, dA = sum dh delta h_t - (1/A) sum (dh rho) B u, and their products
+// dh delta and dh rho also give pc = dh coef (their sum) and q = dh a = dh + A pc: six packed
+// operations per state pair for q, pc and dA.
+// The step-size term uses the same identity: dh_t/ddelta = A a h_{t-1} + a B u = A h_t + B u (ZOH).
 //
 // Reductions: over n inside a channel's lane group (shuffle transposition); over d by a
 // shuffle transposition across the warp's channels, a fixed-order cross-warp sum in shared
@@ -252,7 +256,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
   const size_t bsd = (size_t)b * p.nseg + seg;            // (batch, segment) partial group
   const size_t pbd = (bsd * p.D + d) * N + nbase;
 
-  float2 dh[NP], dAA[NP];
+  float2 dh[NP], dAA[NP], dAR[NP];
   // the adjoint entering the segment from its right: dlast for the last segment, else the composed
   // adjoint summaries of the segments after it
   const float* const dh_in = (seg == p.nseg - 1) ? (p.dlast != nullptr ? p.dlast + bd : nullptr) : p.seg_dh + pbd;
@@ -263,7 +267,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
     for (int i = 0; i < NP; ++i) dh[i] = bc2(0.f);
   }
 #pragma unroll
-  for (int i = 0; i < NP; ++i) dAA[i] = bc2(0.f);
+  for (int i = 0; i < NP; ++i) dAA[i] = dAR[i] = bc2(0.f);
   float dDacc = 0.0f;
   float dtbacc = 0.0f;         // this thread's share of d loss / d dt_bias for channel dl
   // the gate pass visits elements e = tid + k NT, always channel d0 + tid % DT
@@ -562,18 +566,17 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
             dh[k] = fma2(dys2, Cn[k], dh[k]);
             bC[k] = mul2(dys2, ht);
             if (METHOD == kZOH) {
-              const float2 coef = add2(dt2, cf[k]);                // expm1(z) / A = delta + rho
-              const float2 a = fma2(Ak[k], coef, bc2(1.0f));       // e^z = 1 + A coef
-              const float2 q = mul2(dh[k], a);
-              const float2 sv = mul2(q, fma2(Ak[k], hp, Bu));      // dh dh_t/ddelta
+              // pc = dh coef with coef = expm1(z) / A = delta + rho, from its two parts
+              const float2 dhd = mul2(dh[k], dt2), dhr = mul2(dh[k], cf[k]);
+              const float2 pc = add2(dhd, dhr);
+              const float2 sv = mul2(dh[k], fma2(Ak[k], ht, Bu));  // dh dh_t/ddelta = dh (A h_t + B u)
               ddt = add2(ddt, sv);
-              const float2 pc = mul2(dh[k], coef);                 // dh coef
               duP = fma2(pc, Bn[k], duP);
               bB[k] = mul2(pc, u2);
-              // A dh dh_t/dA = dh (z h_t - rho B u)
-              const float2 zh = mul2(mul2(dt2, Ak[k]), ht);
-              dAA[k] = fma2(dh[k], fma2(make_float2(-cf[k].x, -cf[k].y), Bu, zh), dAA[k]);
-              dh[k] = q;
+              // A dh dh_t/dA = dh (z h_t - rho B u): dA = sum dh delta h_t - (1/A) sum dh rho B u
+              dAA[k] = fma2(dhd, ht, dAA[k]);
+              dAR[k] = fma2(dhr, Bu, dAR[k]);
+              dh[k] = fma2(Ak[k], pc, dh[k]);                      // dh a = dh (1 + A coef)
             } else if (METHOD == kEuler) {
               const float2 q = mul2(dh[k], cf[k]);
               const float2 sv = fma2(mul2(q, Ak[k]), hp, mul2(dh[k], Bu));
@@ -667,7 +670,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
   if (dvalid) {
 #pragma unroll
     for (int k = 0; k < NP; ++k) {
-      const float2 da = (METHOD == kZOH) ? mul2(dAA[k], iA[k]) : dAA[k];
+      const float2 da = (METHOD == kZOH) ? fma2(make_float2(-dAR[k].x, -dAR[k].y), iA[k], dAA[k]) : dAA[k];
       p.part_A[pbd + ((2 * k) ^ perm)] = da.x;
       p.part_A[pbd + ((2 * k + 1) ^ perm)] = da.y;
       if (p.dh0 != nullptr && seg == 0) {
