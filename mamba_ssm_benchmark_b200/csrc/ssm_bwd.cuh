@@ -17,10 +17,10 @@
 //       state-permuted fp32 copies of the B, C tiles (see "state permutation" below);
 //   (3) recomputes the chunk's 16 states in registers from the checkpoint the forward saved
 //       (chunk_states), and keeps each step's discretisation coefficient -- the one MUFU-derived
-//       value the reverse pass needs (ZOH: rho = expm1(delta A) / A - delta, Euler: a, bilinear:
+//       value the reverse pass needs (ZOH: r = A rho = expm1(delta A) - delta A, Euler: a, bilinear:
 //       1 / (1 - delta A / 2)) -- in a thread-private shared-memory slot;
 //   (4) runs the reverse adjoint through those registers, reading the coefficients back instead
-//       of re-evaluating exponentials (ZOH: coef = delta + rho, a = 1 + A coef); the bf16 N = 16
+//       of re-evaluating exponentials (ZOH: coef = delta + r / A, a = 1 + A coef); the bf16 N = 16
 //       layout keeps no cache and re-evaluates them, which fits a third CTA on every SM.
 // Both passes fetch step j+-1's inputs while step j computes, and step j's dB|dC reduction is
 // issued after step j-1's arithmetic, so shared-memory and shuffle latency overlap work.
@@ -33,7 +33,7 @@
 //   ddelta_t[d] += sum_n dh dh_t/ddelta,   du_t[d] += sum_n dh dh_t/du,   dA[d,n] += dh dh_t/dA,
 //   dB_t[n] += sum_d dh dh_t/dB,           dC_t[n] += sum_d dys_t[d] h_t[n]
 // ZOH.  coef = expm1(z) / A (z = delta A) enters through rho = coef - delta = (expm1(z) - z) / A,
-// evaluated without cancellation (zoh_rho below).  With a = 1 + A coef and h_t = a h_{t-1} + coef B u,
+// evaluated without cancellation (zoh_r below).  With a = 1 + A coef and h_t = a h_{t-1} + coef B u,
 //   A dh_t/dA = z a h_{t-1} + B u (delta a - coef) = z h_t - rho B u,
 // an exact identity (delta a - coef = z coef - rho) whose two terms do not cancel: the B u parts of
 // z h_t and rho B u stand about 2 : 1 for small z.  So dA = (sum_t dh_t (z h_t - rho B u)) / A costs
@@ -41,9 +41,9 @@
 // reference evaluates f(z) = (z e^z - expm1 z) / z^2 with a series branch
 // (kernels/triton_scan.py:199-202) and forming A dA as delta dh/ddelta - coef B u would lose about
 // 1e-7 / |A| relative (1e-2 at |A| = 1e-3 in the transient of small steps).  In the reverse pass the
-// two sums are kept apart, dA = sum dh delta h_t - (1/A) sum (dh rho) B u, and their products
-// dh delta and dh rho also give pc = dh coef (their sum) and q = dh a = dh + A pc: six packed
-// operations per state pair for q, pc and dA.
+// two sums are kept apart, dA = sum dh delta h_t - (1/A^2) sum (dh r) B u with r = A rho (what the
+// recompute pass caches), and their products dh delta and dh r also give pc = dh coef = dh delta +
+// (dh r) / A and q = dh a = dh + A pc: six packed operations per state pair for q, pc and dA.
 // The step-size term uses the same identity: dh_t/ddelta = A a h_{t-1} + a B u = A h_t + B u (ZOH).
 //
 // Reductions: over n inside a channel's lane group (shuffle transposition); over d by a
@@ -175,18 +175,19 @@ __device__ __forceinline__ void bwd_coop_load(const BwdParams& p, unsigned char*
 
 constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v / 2); }
 
-// ZOH's rho = expm1(z) / A - delta (z = delta A, x = z log2 e) for a pair, given a = ex2(x): the part
-// of the input coefficient beyond its leading term, (expm1(z) - z) / A, evaluated without
-// cancellation.  Both candidates are lower bounds of r = expm1(z) - z for every z (as in em1x2):
+// ZOH's r = expm1(z) - z = A rho (z = delta A, x = z log2 e) for a pair, given a = ex2(x): A times the
+// part of the input coefficient beyond its leading term, rho = coef - delta = (expm1(z) - z) / A,
+// evaluated without cancellation (the 1/A is applied where r is used: coef = delta + r / A).  Both
+// candidates are lower bounds of r for every z (as in em1x2):
 // the polynomial z^2/2 + z^3/6 (its remainder e^xi z^4/24 is >= 0) and the biased MUFU value
 // minus z; their maximum is within min(z^4/24, 3.9e-7 e^z) of r.  Relative to coef = delta + rho
 // that is the error bound of em1x2 (7e-6 at most); relative to rho itself (about delta z / 2) it is
 // z^2/12 below |z| = 0.055 and 7.8e-7 / z^2 above, 2.6e-4 at most (the rho B u term of dA).
-__device__ __forceinline__ float2 zoh_rho(float2 x, float2 a, float2 iA) {
+__device__ __forceinline__ float2 zoh_r(float2 x, float2 a) {
   const float2 e = fma2(a, bc2(kEm1Scale), bc2(-1.0f));
   const float2 rp = mul2(mul2(x, x), fma2(x, bc2(kEm1C3), bc2(kEm1C2)));
   const float2 rm = fma2(x, bc2(-kLn2), e);
-  return mul2(make_float2(fmaxf(rp.x, rm.x), fmaxf(rp.y, rm.y)), iA);
+  return make_float2(fmaxf(rp.x, rm.x), fmaxf(rp.y, rm.y));
 }
 
 // G = 2 exists to raise occupancy, so its register budget is capped at two CTAs per SM; the bf16
@@ -391,8 +392,8 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
       if (METHOD == kZOH) {
         const float2 x = mul2(dt2, A2[k]);
         const float2 a = ex2x2(x);
-        cf[k] = zoh_rho(x, a, iA[k]);                           // rho = expm1(delta A) / A - delta
-        hc[k] = fma2(a, hc[k], mul2(add2(dt2, cf[k]), mul2(Bn[k], u2)));
+        cf[k] = zoh_r(x, a);                                    // r = A rho = expm1(delta A) - delta A
+        hc[k] = fma2(a, hc[k], mul2(fma2(cf[k], iA[k], dt2), mul2(Bn[k], u2)));   // coef = delta + r / A
       } else if (METHOD == kEuler) {
         cf[k] = ex2x2(mul2(dt2, A2[k]));                        // a
         hc[k] = fma2(cf[k], hc[k], mul2(dtu2, Bn[k]));
@@ -548,7 +549,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
             for (int k = 0; k < NP; ++k) {
               if (METHOD == kZOH) {
                 const float2 x = mul2(dt2, A2[k]);
-                cf[k] = zoh_rho(x, ex2x2(x), iA[k]);
+                cf[k] = zoh_r(x, ex2x2(x));
               } else if (METHOD == kEuler) {
                 cf[k] = ex2x2(mul2(dt2, A2[k]));
               } else {
@@ -566,14 +567,14 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
             dh[k] = fma2(dys2, Cn[k], dh[k]);
             bC[k] = mul2(dys2, ht);
             if (METHOD == kZOH) {
-              // pc = dh coef with coef = expm1(z) / A = delta + rho, from its two parts
+              // pc = dh coef with coef = expm1(z) / A = delta + r / A, from its two parts
               const float2 dhd = mul2(dh[k], dt2), dhr = mul2(dh[k], cf[k]);
-              const float2 pc = add2(dhd, dhr);
+              const float2 pc = fma2(dhr, iA[k], dhd);
               const float2 sv = mul2(dh[k], fma2(Ak[k], ht, Bu));  // dh dh_t/ddelta = dh (A h_t + B u)
               ddt = add2(ddt, sv);
               duP = fma2(pc, Bn[k], duP);
               bB[k] = mul2(pc, u2);
-              // A dh dh_t/dA = dh (z h_t - rho B u): dA = sum dh delta h_t - (1/A) sum dh rho B u
+              // A dh dh_t/dA = dh (z h_t - rho B u): dA = sum dh delta h_t - (1/A^2) sum dh r B u
               dAA[k] = fma2(dhd, ht, dAA[k]);
               dAR[k] = fma2(dhr, Bu, dAR[k]);
               dh[k] = fma2(Ak[k], pc, dh[k]);                      // dh a = dh (1 + A coef)
@@ -670,7 +671,7 @@ __global__ void __launch_bounds__(Geo<N, G>::NT, BwdSmem<N, G, T>::MINB) ssm_bwd
   if (dvalid) {
 #pragma unroll
     for (int k = 0; k < NP; ++k) {
-      const float2 da = (METHOD == kZOH) ? fma2(make_float2(-dAR[k].x, -dAR[k].y), iA[k], dAA[k]) : dAA[k];
+      const float2 da = (METHOD == kZOH) ? fma2(make_float2(-dAR[k].x, -dAR[k].y), mul2(iA[k], iA[k]), dAA[k]) : dAA[k];
       p.part_A[pbd + ((2 * k) ^ perm)] = da.x;
       p.part_A[pbd + ((2 * k + 1) ^ perm)] = da.y;
       if (p.dh0 != nullptr && seg == 0) {
