@@ -26,7 +26,7 @@ EXPORTED = (
     "ssm_scan_fwd_summary", "ssm_scan_fwd_finish", "ssm_state_update", "ssm_scan_bwd_noalloc",
     "ssm_scan_bwd_summary", "ssm_conv1d_fwd", "ssm_conv1d_bwd_workspace_size", "ssm_conv1d_bwd",
     "selective_scan_fwd", "selective_scan_bwd", "selective_state_update", "ssm_scan_fwd_ex", "ssm_scan_bwd_ex",
-    "ssm_scan_bwd_plan",
+    "ssm_scan_bwd_plan", "ssm_compose_shards",
 )
 
 
@@ -59,6 +59,7 @@ _SIGNATURES = {
     "ssm_scan_fwd_workspace_size": (ctypes.c_int, [_I64, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
     "ssm_scan_bwd_workspace_size": (ctypes.c_int, [_I64, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
     "ssm_scan_bwd_plan": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, ctypes.POINTER(_I32), ctypes.POINTER(_I32)]),
+    "ssm_compose_shards": (ctypes.c_int, [_I32, _I64, _I64, _I64, _P, _P, _P, _I32, _P, _P, _P]),
     "ssm_scan_fwd": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _V, _P, _V, _V, _P, _V, _P,
                                     _V, _V, _P, _P, _P, _SZ, _P]),
     "ssm_scan_fwd_summary": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _V, _P, _V, _P, _P,

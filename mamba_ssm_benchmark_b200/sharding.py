@@ -86,13 +86,31 @@ def exchange_summaries(decay, hend, group=None):
     return allp[:, 0], allp[:, 1]
 
 
+def _compose_on_device(decays, ends, start, reverse):
+    """One ssm_compose_shards launch over CUDA-resident summaries."""
+    W, B, D, N = decays.shape
+    decays = decays.to(torch.float32).contiguous()
+    ends = ends.to(torch.float32).contiguous()
+    start = None if start is None else start.to(torch.float32).contiguous()
+    out = torch.empty_like(ends)
+    last = torch.empty_like(ends[0])
+    with torch.cuda.device(decays.device):
+        rc = nat.lib().ssm_compose_shards(W, B, D, N, nat.ptr(decays), nat.ptr(ends), nat.ptr(start), int(reverse),
+                                          nat.ptr(out), nat.ptr(last), nat.stream_of(decays.device))
+    nat.check(rc, "ssm_compose_shards")
+    return out, last
+
+
 def compose_prefix(decays, hends, h0=None):
     """Carried-in state of every shard and the final state of the whole sequence.
 
     decays, hends: (W, B, D, N) summaries of shards 0..W-1 in sequence order; h0: (B, D, N) or None.
     h_in[0] = h0, h_in[r] = decays[r-1] * h_in[r-1] + hends[r-1]; last = the same step past shard W-1.
     (The combine of chunk ends in models/scan.py:160-164, written as a left-to-right walk because W
-    is at most the number of GPUs.)"""
+    is at most the number of GPUs.)  CUDA tensors: one ssm_compose_shards launch; CPU tensors (the
+    host-side protocol on gloo ranks): the same walk in torch."""
+    if decays.is_cuda:
+        return _compose_on_device(decays, hends, h0, False)
     W = decays.shape[0]
     h = torch.zeros_like(hends[0]) if h0 is None else h0.to(torch.float32)
     h_in = torch.empty_like(hends)
@@ -197,7 +215,9 @@ def compose_suffix(decays, dstarts, dlast=None):
     decays, dstarts: (W, B, D, N) adjoint summaries of shards 0..W-1 in sequence order;
     dlast: (B, D, N) gradient of the whole sequence's final state, or None.
     dl_in[W-1] = dlast, dl_in[r] = dstarts[r+1] + decays[r+1] * dl_in[r+1];
-    dh0 = dstarts[0] + decays[0] * dl_in[0]."""
+    dh0 = dstarts[0] + decays[0] * dl_in[0].  CUDA tensors: one ssm_compose_shards launch (reverse)."""
+    if decays.is_cuda:
+        return _compose_on_device(decays, dstarts, dlast, True)
     W = decays.shape[0]
     g = torch.zeros_like(dstarts[0]) if dlast is None else dlast.to(torch.float32)
     dl_in = torch.empty_like(dstarts)

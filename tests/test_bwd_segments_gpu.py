@@ -23,6 +23,8 @@ CASES = [
     (2, 1000, 96, 8, torch.float32, "euler", True),
     (1, 777, 40, 16, torch.float32, "bilinear", True),
     (3, 520, 33, 4, torch.float32, "zoh", True),
+    (1, 600, 64, 32, torch.float32, "zoh", True),
+    (1, 600, 40, 64, torch.float32, "euler", False),   # N = 64: coefficients evaluated again, no cache
 ]
 
 

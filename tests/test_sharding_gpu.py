@@ -129,6 +129,21 @@ def test_sequence_shards_backward_single_gpu(shards, method):
         assert O.normwise_error(got[k], ref[k]) < 1e-3, k
 
 
+@pytest.mark.parametrize("W", [1, 3, 8])
+def test_compose_kernel_matches_the_walk(W):
+    """ssm_compose_shards (CUDA) against the torch walk of compose_prefix / compose_suffix (CPU)."""
+    g = torch.Generator().manual_seed(W)
+    dec = torch.rand(W, 2, 40, 16, generator=g)
+    end = torch.randn(W, 2, 40, 16, generator=g)
+    st = torch.randn(2, 40, 16, generator=g)
+    for start in (None, st):
+        for fn in (sharding.compose_prefix, sharding.compose_suffix):
+            want = fn(dec, end, start)
+            got = fn(dec.to(DEV), end.to(DEV), None if start is None else start.to(DEV))
+            for a, b in zip(got, want):
+                assert torch.allclose(a.cpu(), b, rtol=1e-6, atol=1e-6)
+
+
 def test_sequence_sharded_scan_without_process_group():
     """Outside torch.distributed the sharded scan is the whole-sequence scan."""
     B, L, D, N = 1, 1024, 64, 16
