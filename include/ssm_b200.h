@@ -123,7 +123,9 @@ SSM_API int ssm_scan_fwd(int64_t B, int64_t L, int64_t D, int64_t N, int32_t met
  * ------------------------------------------------------------------------------- */
 SSM_API int ssm_scan_bwd_workspace_size(int64_t B, int64_t L, int64_t D, int64_t N, size_t* bytes);
 
-/* Composition of W shard summaries, each (W, B, D, N) float32 in shard order:
+/* Composition of W shard summaries in shard order, float32: shard r's (B, D, N) block of decay and
+ * of end starts r * shard_stride elements after decay / end (0: B*D*N, packed; both arrays may be
+ * interleaved blocks of one all-gathered buffer); out is (W, B, D, N) packed.
  *   out[r] = carry;  carry = decay[r] * carry + end[r]   (r = 0..W-1; reverse != 0: r = W-1..0)
  * from carry = start (B, D, N) or zeros; last (B, D, N, or NULL) gets the final carry.  Forward:
  * decay/end = the shards' ssm_scan_fwd_summary outputs, out = the state entering every shard,
@@ -131,7 +133,8 @@ SSM_API int ssm_scan_bwd_workspace_size(int64_t B, int64_t L, int64_t D, int64_t
  * outputs, start = dlast, out = the adjoint entering every shard, last = dh0.  Replaces the chunk-end
  * combine of models/scan.py:160-164 across GPUs (the reference runs on one GPU). */
 SSM_API int ssm_compose_shards(int32_t W, int64_t B, int64_t D, int64_t N, const float* decay, const float* end,
-                               const float* start, int32_t reverse, float* out, float* last, void* stream);
+                               int64_t shard_stride, const float* start, int32_t reverse, float* out, float* last,
+                               void* stream);
 
 /* The backward's sequence split for a shape on the current device: *nseg segments of *seg_len
  * steps (a multiple of 16; *nseg = 1: no split).  The reference's backward runs one program per

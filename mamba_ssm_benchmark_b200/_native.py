@@ -59,7 +59,7 @@ _SIGNATURES = {
     "ssm_scan_fwd_workspace_size": (ctypes.c_int, [_I64, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
     "ssm_scan_bwd_workspace_size": (ctypes.c_int, [_I64, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
     "ssm_scan_bwd_plan": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, ctypes.POINTER(_I32), ctypes.POINTER(_I32)]),
-    "ssm_compose_shards": (ctypes.c_int, [_I32, _I64, _I64, _I64, _P, _P, _P, _I32, _P, _P, _P]),
+    "ssm_compose_shards": (ctypes.c_int, [_I32, _I64, _I64, _I64, _P, _P, _I64, _P, _I32, _P, _P, _P]),
     "ssm_scan_fwd": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _V, _P, _V, _V, _P, _V, _P,
                                     _V, _V, _P, _P, _P, _SZ, _P]),
     "ssm_scan_fwd_summary": (ctypes.c_int, [_I64, _I64, _I64, _I64, _I32, _V, _V, _P, _V, _P, _P,

@@ -23,7 +23,7 @@
 namespace ssm {
 cudaError_t launch_carry(const CarryParams& p, cudaStream_t stream);
 cudaError_t launch_compose(const float* decay, const float* end, const float* start, float* out, float* last, int W,
-                           long long elems, int reverse, cudaStream_t stream);
+                           long long elems, long long stride, int reverse, cudaStream_t stream);
 cudaError_t launch_update(int N, bool bf16, const UpdParams& p, cudaStream_t stream);
 }  // namespace ssm
 
@@ -475,14 +475,18 @@ int ssm_scan_bwd_workspace_size(int64_t B, int64_t L, int64_t D, int64_t N, size
 }
 
 int ssm_compose_shards(int32_t W, int64_t B, int64_t D, int64_t N, const float* decay, const float* end,
-                       const float* start, int32_t reverse, float* out, float* last, void* stream) {
+                       int64_t shard_stride, const float* start, int32_t reverse, float* out, float* last,
+                       void* stream) {
+  const int64_t elems = B * D * N;
+  if (shard_stride == 0) shard_stride = elems;
+  if (shard_stride < elems) return fail(SSM_ERR_INVALID, "shard_stride %lld is below B*D*N", (long long)shard_stride);
   if (W < 1 || B < 1 || D < 1 || N < 1)
     return fail(SSM_ERR_INVALID, "shape W=%d B=%lld D=%lld N=%lld must be positive", (int)W, (long long)B,
                 (long long)D, (long long)N);
   if (decay == nullptr || end == nullptr || out == nullptr)
     return fail(SSM_ERR_INVALID, "decay, end and out are required");
-  cudaError_t e = launch_compose(decay, end, start, out, last, (int)W, (long long)(B * D * N), reverse ? 1 : 0,
-                                 static_cast<cudaStream_t>(stream));
+  cudaError_t e = launch_compose(decay, end, start, out, last, (int)W, (long long)elems, (long long)shard_stride,
+                                 reverse ? 1 : 0, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "compose launch");
   return SSM_OK;
 }

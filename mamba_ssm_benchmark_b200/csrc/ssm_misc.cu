@@ -67,7 +67,8 @@ cudaError_t launch_carry(const CarryParams& p, cudaStream_t stream) {
   return launch_pdl(ssm_carry_kernel, dim3((unsigned)((total + 31) / 32)), dim3(32, kCarryGroups), 0, stream, p);
 }
 
-// Composition of W shard summaries laid out (W, B, D, N), one thread per (b, d, n):
+// Composition of W shard summaries (shard r's (B, D, N) block at r * stride elements), one thread
+// per (b, d, n):
 //   out[r] = carry;  carry = decay[r] * carry + end[r]        (r = 0 .. W-1, or W-1 .. 0 reversed)
 // with carry starting at start (or 0); the final carry goes to last.  The cross-GPU form of the
 // segment carry above: the prefix of the sequence-sharded forward (the carried-in state of every
@@ -75,22 +76,23 @@ cudaError_t launch_carry(const CarryParams& p, cudaStream_t stream) {
 // two small tensor operations per shard.
 __global__ void ssm_compose_kernel(const float* __restrict__ decay, const float* __restrict__ end,
                                    const float* __restrict__ start, float* __restrict__ out,
-                                   float* __restrict__ last, int W, long long elems, int reverse) {
+                                   float* __restrict__ last, int W, long long elems, long long stride, int reverse) {
   const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (i >= elems) return;
   float carry = start != nullptr ? start[i] : 0.0f;
   for (int k = 0; k < W; ++k) {
-    const long long o = (long long)(reverse ? W - 1 - k : k) * elems + i;
-    out[o] = carry;
+    const long long r = reverse ? W - 1 - k : k;
+    const long long o = r * stride + i;
+    out[r * elems + i] = carry;
     carry = fmaf(decay[o], carry, end[o]);
   }
   if (last != nullptr) last[i] = carry;
 }
 
 cudaError_t launch_compose(const float* decay, const float* end, const float* start, float* out, float* last, int W,
-                           long long elems, int reverse, cudaStream_t stream) {
+                           long long elems, long long stride, int reverse, cudaStream_t stream) {
   const unsigned blocks = (unsigned)((elems + 255) / 256);
-  ssm_compose_kernel<<<blocks, 256, 0, stream>>>(decay, end, start, out, last, W, elems, reverse);
+  ssm_compose_kernel<<<blocks, 256, 0, stream>>>(decay, end, start, out, last, W, elems, stride, reverse);
   return cudaGetLastError();
 }
 

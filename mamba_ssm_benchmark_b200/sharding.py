@@ -75,28 +75,41 @@ def reduce_shared_grads(grads, group=None):
 # ------------------------------------------------------------------------------------------------
 def exchange_summaries(decay, hend, group=None):
     """All-gather every rank's (decay, hend) summary: returns (decays, hends), each (W, B, D, N),
-    indexed by rank (= shard position along the sequence)."""
-    pack = torch.stack((decay.to(torch.float32), hend.to(torch.float32))).contiguous()
+    indexed by rank (= shard position along the sequence).  One collective into one (W, 2, B, D, N)
+    buffer; the two results are views of it (``compose_prefix`` reads them in place).  A summary
+    that is already the (2, B, D, N) pack (``SequenceShard.summary``) is sent without a copy."""
+    base = decay._base
+    if (base is not None and base is hend._base and base.dim() == decay.dim() + 1 and base.shape[0] == 2
+            and base.dtype == torch.float32 and base.is_contiguous()
+            and decay.data_ptr() == base.data_ptr() and hend.data_ptr() == base[1].data_ptr()):
+        pack = base
+    else:
+        pack = torch.stack((decay.to(torch.float32), hend.to(torch.float32))).contiguous()
     if not dist.is_initialized() or dist.get_world_size(group) == 1:
         return pack[0:1], pack[1:2]
     world = dist.get_world_size(group)
-    parts = [torch.empty_like(pack) for _ in range(world)]
-    dist.all_gather(parts, pack, group=group)
-    allp = torch.stack(parts)
+    allp = torch.empty((world,) + tuple(pack.shape), dtype=pack.dtype, device=pack.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(allp, pack, group=group)
+    else:                                   # gloo (CPU ranks): the list form
+        dist.all_gather(list(allp.unbind(0)), pack, group=group)
     return allp[:, 0], allp[:, 1]
 
 
 def _compose_on_device(decays, ends, start, reverse):
     """One ssm_compose_shards launch over CUDA-resident summaries."""
     W, B, D, N = decays.shape
-    decays = decays.to(torch.float32).contiguous()
-    ends = ends.to(torch.float32).contiguous()
+    blocks_ok = lambda t: t.dtype == torch.float32 and t[0].is_contiguous() and t.stride(0) == decays.stride(0)
+    if not (blocks_ok(decays) and blocks_ok(ends) and decays.stride(0) >= B * D * N):
+        decays = decays.to(torch.float32).contiguous()
+        ends = ends.to(torch.float32).contiguous()
+    stride = decays.stride(0) if W > 1 else B * D * N
     start = None if start is None else start.to(torch.float32).contiguous()
-    out = torch.empty_like(ends)
-    last = torch.empty_like(ends[0])
+    out = torch.empty((W, B, D, N), dtype=torch.float32, device=decays.device)
+    last = torch.empty((B, D, N), dtype=torch.float32, device=decays.device)
     with torch.cuda.device(decays.device):
-        rc = nat.lib().ssm_compose_shards(W, B, D, N, nat.ptr(decays), nat.ptr(ends), nat.ptr(start), int(reverse),
-                                          nat.ptr(out), nat.ptr(last), nat.stream_of(decays.device))
+        rc = nat.lib().ssm_compose_shards(W, B, D, N, nat.ptr(decays), nat.ptr(ends), stride, nat.ptr(start),
+                                          int(reverse), nat.ptr(out), nat.ptr(last), nat.stream_of(decays.device))
     nat.check(rc, "ssm_compose_shards")
     return out, last
 
@@ -155,7 +168,8 @@ class SequenceShard:
 
     def summary(self):
         Bsz, L, Dch, N = self.shape
-        decay, hend = self._state(), self._state()
+        pack = torch.empty((2, Bsz, Dch, N), dtype=torch.float32, device=self.dev)   # what exchange_summaries sends
+        decay, hend = pack[0], pack[1]
         with torch.cuda.device(self.dev):
             rc = nat.lib().ssm_scan_fwd_summary(Bsz, L, Dch, N, nat.METHODS[self.method], nat.view3(self.x),
                                                 nat.view3(self.delta), nat.ptr(self.A), nat.view3(self.Bm),
