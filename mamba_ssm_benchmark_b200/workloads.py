@@ -107,6 +107,10 @@ NCU_TRAFFIC = {
     # scaled by 8/3 (every byte either kernel moves is proportional to the batch)
     ("ssm_scan_fwd", "cfg3_fwdbwd_bf16_B8_L8192_D5120_N16"): 4765744000,
     ("ssm_scan_bwd", "cfg3_fwdbwd_bf16_B8_L8192_D5120_N16"): 7996509333,
+    # profiles/fwd_segmented_cfg2_cfg0.md: one ssm_scan_fwd call = summary pass + carry + main pass
+    # (the three kernels' DRAM bytes summed, mean of three calls)
+    ("ssm_scan_fwd", "cfg2_fwd_fp32_B1_L131072_D512_N16"): 1653311061,
+    ("ssm_scan_fwd", "cfg0_fwd_fp32_B1_L4096_D512_N16"): 46085973,
 }
 
 
