@@ -100,9 +100,9 @@ def algorithmic_bytes(B, L, D, N, elem_bytes, fused=True, backward=True):
 NCU_TRAFFIC = {
     # profiles/bwd_kernel_cfg1_fwdbwd_fp32_B16_L512_D512_N16.md (the backward kernel; its finalize
     # reads the per-CTA partials mostly from L2)
-    ("ssm_scan_bwd", "cfg1_fwdbwd_fp32_B16_L512_D512_N16"): 133577216,
+    ("ssm_scan_bwd", "cfg1_fwdbwd_fp32_B16_L512_D512_N16"): 133680128,
     # profiles/fwd_kernel_cfg1_fwdbwd_fp32_B16_L512_D512_N16.md
-    ("ssm_scan_fwd", "cfg1_fwdbwd_fp32_B16_L512_D512_N16"): 61051136,
+    ("ssm_scan_fwd", "cfg1_fwdbwd_fp32_B16_L512_D512_N16"): 60009472,
     # profiles/fwdbwd_kernels_cfg3_bf16_shape3x8192x5120.md: three of the eight batch rows captured,
     # scaled by 8/3 (every byte either kernel moves is proportional to the batch)
     ("ssm_scan_fwd", "cfg3_fwdbwd_bf16_B8_L8192_D5120_N16"): 4765744000,
