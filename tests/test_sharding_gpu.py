@@ -12,6 +12,7 @@ import sys
 import pytest
 import torch
 
+import scan_harness as H
 from mamba_ssm_benchmark_b200 import _native as nat
 from mamba_ssm_benchmark_b200 import selective_scan_fused, sharding
 from mamba_ssm_benchmark_b200.workloads import make_inputs
@@ -127,6 +128,40 @@ def test_sequence_shards_backward_single_gpu(shards, method):
     assert O.normwise_error(torch.cat(ys, 1), yr) < 1e-4
     for k in keys:
         assert O.normwise_error(got[k], ref[k]) < 1e-3, k
+
+
+@pytest.mark.parametrize("shards", [2, 3])
+def test_sequence_shards_backward_bf16(shards):
+    """bf16 activations through the sharded backward (adjoint summaries, suffix, per-shard backward):
+    the stitched gradients against the oracle on the same bf16-rounded inputs, at the bf16 tolerance."""
+    B, L, D, N = 2, 900, 64, 16
+    ins = make_inputs(B, L, D, N, seed=3 + shards, dist="config", h0=True, dlast=True)
+    for k in ("u", "delta", "Bm", "Cm", "z", "dy"):
+        ins[k] = ins[k].to(torch.bfloat16).float()
+    dev = {k: (v.to(DEV) if v is not None else None) for k, v in ins.items()}
+    act = {k: dev[k].to(torch.bfloat16) for k in ("u", "delta", "Bm", "Cm", "z", "dy")}
+    bounds = [sharding.shard_range(L, shards, r) for r in range(shards)]
+    pieces = [sharding.SequenceShard(act["u"][:, lo:hi], act["delta"][:, lo:hi], dev["A"], act["Bm"][:, lo:hi],
+                                     act["Cm"][:, lo:hi], "zoh", D=dev["Dskip"], z=act["z"][:, lo:hi])
+              for lo, hi in bounds]
+    sums = [p.summary() for p in pieces]
+    h_in, _ = sharding.compose_prefix(torch.stack([s[0] for s in sums]), torch.stack([s[1] for s in sums]), dev["h0"])
+    ys = [p.finish(h_in[r], save=True)[0] for r, p in enumerate(pieces)]
+    adj = [p.adjoint_summary(act["dy"][:, lo:hi]) for p, (lo, hi) in zip(pieces, bounds)]
+    dl_in, dh0 = sharding.compose_suffix(torch.stack([a[0] for a in adj]), torch.stack([a[1] for a in adj]),
+                                         dev["dlast"])
+    g = [p.backward(act["dy"][:, lo:hi], dl_in[r]) for r, (p, (lo, hi)) in enumerate(zip(pieces, bounds))]
+    got = {"u": torch.cat([x[0] for x in g], 1), "delta": torch.cat([x[1] for x in g], 1), "A": sum(x[2] for x in g),
+           "Bm": torch.cat([x[3] for x in g], 1), "Cm": torch.cat([x[4] for x in g], 1), "h0": dh0,
+           "Dskip": sum(x[6] for x in g), "z": torch.cat([x[7] for x in g], 1)}
+    keys = ("u", "delta", "A", "Bm", "Cm", "Dskip", "z", "h0")
+    cpu = {k: ins[k].clone().requires_grad_() for k in keys}
+    yr, lr = O.selective_scan_fused(cpu["u"], cpu["delta"], cpu["A"], cpu["Bm"], cpu["Cm"], h0=cpu["h0"],
+                                    Dskip=cpu["Dskip"], z=cpu["z"])
+    ref = dict(zip(keys, torch.autograd.grad((yr, lr), [cpu[k] for k in keys], (ins["dy"], ins["dlast"]))))
+    assert O.normwise_error(torch.cat(ys, 1).float().cpu(), yr.detach()) < H.BF16_TOL
+    for k in keys:
+        assert O.normwise_error(got[k].float().cpu(), ref[k]) < H.BF16_TOL, k
 
 
 @pytest.mark.parametrize("W", [1, 3, 8])

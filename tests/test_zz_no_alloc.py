@@ -66,8 +66,10 @@ def _backward(ins, cs, yg, B, L, D, N, noalloc, out=None):
 
 
 @pytest.mark.parametrize("shape,dtype", [((2, 100, 64, 16), torch.float32), ((16, 512, 512, 16), torch.float32),
-                                         ((3, 37, 50, 8), torch.float32), ((2, 300, 96, 16), torch.bfloat16)],
-                         ids=["2x100x64x16", "16x512x512x16", "3x37x50x8", "2x300x96x16-bf16"])
+                                         ((3, 37, 50, 8), torch.float32), ((2, 300, 96, 16), torch.bfloat16),
+                                         ((1, 2048, 64, 16), torch.float32)],
+                         ids=["2x100x64x16", "16x512x512x16", "3x37x50x8", "2x300x96x16-bf16",
+                              "1x2048x64x16-split"])
 def test_noalloc_backward_matches_workspace_backward_twice(shape, dtype):
     B, L, D, N = shape
     assert nat.bwd_workspace_bytes(B, L, D, N) <= 32 << 20
